@@ -1,0 +1,260 @@
+"""Generate golden vectors by running the reference StickyKV code on seeded inputs.
+
+Run in a container where the reference checkout is available:
+
+    python tests/golden/make_golden.py [--ref /root/reference]
+
+It imports the reference read-only (``sys.path``) and writes small ``.npz`` /
+``.json`` fixtures next to this script.  The fixtures are committed; nothing at
+test time reads the reference tree.
+
+Fixtures:
+  resolve.json         WindowedCacheConfig.resolve on the reference KAT
+                       geometries and on the five benchmark geometries
+  scorer.npz           compute_window_scores / reduce_token_scores_to_windows
+  policy.npz           EvictionPolicy.compute_retain_window_indices +
+                       expand_to_token_indices on tie-free fp32 scores
+  rerotate_<dt>.npz    CacheState.slice_and_keep + rerotate_keys with a HF
+                       LlamaRotaryEmbedding (theta 5e5), dt in f32/bf16/f16
+  cache_drive_<dt>.npz WindowedCache.update driven through prefill + 40 decode
+                       steps (5 evictions) with hook-style scores each step
+  eager_decode_<dt>.npz transformers eager_attention_forward +
+                       compute_window_scores for one decode query
+  prefill_scores.npz   the flash hook's chunked causal scoring math
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+@dataclass
+class FakeModelConfig:
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    hidden_size: int = 4096
+    head_dim: int = 128
+    num_hidden_layers: int = 32
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().to(torch.float32).cpu().numpy() if t.is_floating_point() else t.cpu().numpy()
+
+
+def rope_module(theta: float, head_dim: int, max_pos: int = 40000):
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    cfg = LlamaConfig(hidden_size=head_dim * 4, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=head_dim, rope_theta=theta, max_position_embeddings=max_pos)
+    return LlamaRotaryEmbedding(config=cfg)
+
+
+def rope_table(rope, n_pos: int, head_dim: int):
+    cos, sin = rope(torch.zeros(1, 1, 1, head_dim), torch.arange(n_pos)[None])
+    return to_np(cos[0]), to_np(sin[0])
+
+
+def gen_resolve(WindowedCacheConfig):
+    cases = []
+    # reference KATs (tests/test_windowed_cache.py:91-188)
+    for (ws, s, loc, bud, P, M, mc, dt) in [
+        (8, 4, 0.25, 0.50, 100, 128, FakeModelConfig(), "f16"),
+        (8, 4, 0.10, 0.50, 100, 128, FakeModelConfig(), "f16"),
+        (8, 4, 16, 0.40, 100, 100, FakeModelConfig(32, 8, 4096, 128), "f16"),
+        (8, 4, 8, 0.20, 200, 128, FakeModelConfig(), "f32"),
+        (8, 4, 8, 0.60, 200, 128, FakeModelConfig(), "f16"),
+        (8, 4, 8, 1.0, 200, 128, FakeModelConfig(), "f32"),
+        (8, 4, 8, 0.12, 100, 50, FakeModelConfig(), "f16"),
+        (1, 0, 1, 0.375, 8, 0, FakeModelConfig(), "f32"),
+        # the five benchmark geometries
+        (8, 4, 0.25, 0.40, 512, 50, FakeModelConfig(4, 2, 256, 64), "f32"),
+        (8, 4, 0.25, 0.40, 4096, 0, FakeModelConfig(32, 8, 2048, 64), "f16"),
+        (8, 4, 0.25, 0.40, 8192, 0, FakeModelConfig(32, 8, 2048, 64), "f16"),
+        (8, 4, 0.25, 0.40, 16384, 0, FakeModelConfig(32, 8, 2048, 64), "f16"),
+        (8, 4, 0.25, 0.40, 32768, 0, FakeModelConfig(32, 8, 2048, 64), "f16"),
+        (8, 4, 0.25, 0.40, 16384, 0, FakeModelConfig(32, 8, 2048, 64), "bf16"),
+        (8, 4, 0.25, 0.40, 8192, 256, FakeModelConfig(32, 8, 2048, 64), "bf16"),
+        (8, 4, 0.25, 0.25, 32768, 128, FakeModelConfig(32, 8, 4096, 128), "bf16"),
+        (5, 3, 0.33, 0.7, 97, 13, FakeModelConfig(6, 3, 96, 16), "f32"),
+    ]:
+        r = WindowedCacheConfig(window_size=ws, num_sink_tokens=s, local_window_size=loc,
+                                cache_budget=bud).resolve(P, mc, DT[dt], M)
+        cases.append(dict(window_size=ws, num_sink_tokens=s, local_window_size=loc,
+                          cache_budget=bud, prefill_len=P, max_tokens=M,
+                          num_kv_heads=mc.num_key_value_heads, head_dim=mc.head_dim,
+                          dtype=dt, resolved=r.__dict__))
+    with open(os.path.join(HERE, "resolve.json"), "w") as f:
+        json.dump(cases, f, indent=1)
+
+
+def gen_scorer(scorer):
+    g = torch.Generator().manual_seed(11)
+    attn = torch.randn(2, 4, 3, 37, generator=g).softmax(-1)
+    out = {"attn": to_np(attn)}
+    for (s, ws) in [(4, 5), (0, 8), (4, 8), (3, 1)]:
+        out[f"ws_{s}_{ws}"] = to_np(scorer.compute_window_scores(attn, s, ws))
+    tok = torch.rand(3, 5, 29, generator=g)
+    out["tok"] = to_np(tok)
+    out["tok_4_8"] = to_np(scorer.reduce_token_scores_to_windows(tok, 4, 8))
+    np.savez_compressed(os.path.join(HERE, "scorer.npz"), **out)
+
+
+def gen_policy(ResolvedConfig, EvictionPolicy):
+    g = torch.Generator().manual_seed(12)
+    out = {}
+    cases = []
+    for ci, (B, Hq, W, k, loc_w, ws, s, extra) in enumerate([
+            (3, 4, 20, 5, 3, 8, 4, 0), (2, 8, 9, 0, 2, 8, 4, 3), (2, 4, 6, 9, 2, 8, 4, 5),
+            (4, 32, 64, 17, 10, 8, 4, 1), (1, 4, 7, 2, 1, 5, 3, 2)]):
+        scores = torch.rand(B, Hq, W, generator=g)
+        res = ResolvedConfig(window_size=ws, num_sink_tokens=s, local_tokens=loc_w * ws,
+                             top_k_windows=k, bytes_per_token=4, total_budget_bytes=0,
+                             total_budget_tokens=0)
+        pol = EvictionPolicy(res)
+        total = s + (W - 1) * ws + extra if extra else s + W * ws
+        pol.initialize_after_prefill(total)
+        ret = pol.compute_retain_window_indices(scores)
+        tok = pol.expand_to_token_indices(ret)
+        out[f"scores_{ci}"] = to_np(scores)
+        out[f"ret_{ci}"] = to_np(ret)
+        out[f"tok_{ci}"] = to_np(tok)
+        cases.append([k, loc_w, ws, s, total])
+    out["cases"] = np.array(cases, dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "policy.npz"), **out)
+
+
+def gen_rerotate(CacheState):
+    rope = rope_module(500000.0, 64)
+    cos, sin = rope_table(rope, 1000, 64)
+    for dt in ("f32", "bf16", "f16"):
+        g = torch.Generator().manual_seed(13)
+        B, H, T, D = 2, 3, 40, 64
+        k = torch.randn(B, H, T, D, generator=g).to(DT[dt])
+        v = torch.randn(B, H, T, D, generator=g).to(DT[dt])
+        pos = torch.stack([torch.sort(torch.randperm(1000, generator=g)[:T])[0] for _ in range(B)])
+        keep = torch.stack([torch.sort(torch.randperm(T, generator=g)[:25])[0] for _ in range(B)])
+        st = CacheState()
+        st.key_states, st.value_states, st.position_ids = k.clone(), v.clone(), pos.clone()
+        old = st.position_ids.gather(1, keep).clone()
+        st.slice_and_keep(keep)
+        st.rerotate_keys(rope, old)
+        np.savez_compressed(os.path.join(HERE, f"rerotate_{dt}.npz"), k=to_np(k), v=to_np(v),
+                            pos=to_np(pos), keep=to_np(keep), cos=cos, sin=sin,
+                            k_out=to_np(st.key_states), v_out=to_np(st.value_states),
+                            pos_out=to_np(st.position_ids))
+
+
+def gen_cache_drive(WindowedCache, WindowedCacheConfig):
+    rope = rope_module(10000.0, 64)
+    cos, sin = rope_table(rope, 512, 64)
+    for dt in ("f32", "bf16"):
+        g = torch.Generator().manual_seed(14)
+        B, Hkv, Hq, D, P, M = 2, 2, 4, 64, 100, 40
+        mc = FakeModelConfig(Hq, Hkv, Hq * D, D)
+        cfg = WindowedCacheConfig(window_size=8, num_sink_tokens=4, local_window_size=0.25,
+                                  cache_budget=0.5)
+        cache = WindowedCache(config=cfg, prefill_len=P, model_config=mc, kv_dtype=DT[dt],
+                              rope_module=rope, num_layers=1, max_tokens=M)
+        rec = {"cos": cos, "sin": sin}
+        k = torch.randn(B, Hkv, P, D, generator=g).to(DT[dt])
+        v = torch.randn(B, Hkv, P, D, generator=g).to(DT[dt])
+        rec["k_0"], rec["v_0"] = to_np(k), to_np(v)
+        cache.update(k, v, 0)
+        n = cache.get_seq_length(0)
+        sc = torch.rand(B, Hq, math.ceil((n - 4) / 8), generator=g)
+        rec["s_0"] = to_np(sc)
+        cache.cache_kwargs[0]["window_scores"] = sc
+        for t in range(1, M + 1):
+            k = torch.randn(B, Hkv, 1, D, generator=g).to(DT[dt])
+            v = torch.randn(B, Hkv, 1, D, generator=g).to(DT[dt])
+            rec[f"k_{t}"], rec[f"v_{t}"] = to_np(k), to_np(v)
+            cache.update(k, v, 0)
+            n = cache.get_seq_length(0)
+            st = cache._states[0]
+            rec[f"len_{t}"] = np.array(n)
+            rec[f"ids_{t}"] = to_np(st.original_window_ids)
+            sc = torch.rand(B, Hq, math.ceil((n - 4) / 8), generator=g)
+            rec[f"s_{t}"] = to_np(sc)
+            cache.cache_kwargs[0]["window_scores"] = sc
+        st = cache._states[0]
+        rec["final_k"], rec["final_v"] = to_np(st.key_states), to_np(st.value_states)
+        rec["final_scores"] = to_np(st.window_scores)
+        rec["final_ids"] = to_np(st.original_window_ids)
+        rec["final_pos"] = to_np(st.position_ids)
+        rec["meta"] = np.array([B, Hkv, Hq, D, P, M])
+        np.savez_compressed(os.path.join(HERE, f"cache_drive_{dt}.npz"), **rec)
+
+
+def gen_eager_decode(scorer):
+    from transformers.models.llama.modeling_llama import eager_attention_forward
+
+    class Mod(torch.nn.Module):
+        num_key_value_groups = 4
+
+    for dt in ("f32", "f16"):
+        g = torch.Generator().manual_seed(15)
+        B, Hq, Hkv, S, D = 2, 8, 2, 77, 64
+        q = torch.randn(B, Hq, 1, D, generator=g).to(DT[dt])
+        k = torch.randn(B, Hkv, S, D, generator=g).to(DT[dt])
+        v = torch.randn(B, Hkv, S, D, generator=g).to(DT[dt])
+        out, w = eager_attention_forward(Mod().eval(), q, k, v, None, scaling=D ** -0.5)
+        sc = scorer.compute_window_scores(w, 4, 8)
+        np.savez_compressed(os.path.join(HERE, f"eager_decode_{dt}.npz"), q=to_np(q[:, :, 0]),
+                            k=to_np(k), v=to_np(v), out=to_np(out[:, 0]), scores=to_np(sc))
+
+
+def gen_prefill_scores(scorer):
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(16)
+    B, Hq, Hkv, T, D = 1, 4, 2, 45, 16
+    q = torch.randn(B, Hq, T, D, generator=g)
+    k = torch.randn(B, Hkv, T, D, generator=g)
+    kx = k.repeat_interleave(Hq // Hkv, dim=1)
+    scaling = D ** -0.5
+    # modules/windowed_cache/hooks.py:258-289 with chunk 16
+    token_scores = torch.zeros(B, Hq, T)
+    for start in range(0, T, 16):
+        end = min(start + 16, T)
+        aw = torch.matmul(q[:, :, start:end], kx.transpose(-2, -1)) * scaling
+        causal = torch.triu(torch.ones(end - start, T, dtype=torch.bool), diagonal=T - T + start + 1)
+        aw = aw.masked_fill(causal, float("-inf"))
+        token_scores += F.softmax(aw, dim=-1, dtype=torch.float32).sum(dim=-2)
+    sc = scorer.reduce_token_scores_to_windows(token_scores, 4, 8)
+    np.savez_compressed(os.path.join(HERE, "prefill_scores.npz"), q=to_np(q), k=to_np(k),
+                        scores=to_np(sc))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    from modules.windowed_cache import scorer
+    from modules.windowed_cache.cache import WindowedCache
+    from modules.windowed_cache.config import ResolvedConfig, WindowedCacheConfig
+    from modules.windowed_cache.policy import EvictionPolicy
+    from modules.windowed_cache.state import CacheState
+    torch.set_num_threads(1)
+    gen_resolve(WindowedCacheConfig)
+    gen_scorer(scorer)
+    gen_policy(ResolvedConfig, EvictionPolicy)
+    gen_rerotate(CacheState)
+    gen_cache_drive(WindowedCache, WindowedCacheConfig)
+    gen_eager_decode(scorer)
+    gen_prefill_scores(scorer)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
