@@ -1,0 +1,403 @@
+"""Benchmark of the windowed-eviction decode path on B200.
+
+Workload (one "step"): one decode step of one attention layer of the
+isolated decode-attention geometry at 32k context — batch 16, 32 query heads,
+8 KV heads (GQA 4), head_dim 64, fp16, retained cache 0.40 x 32768 = 13100
+tokens (4 fp16 sinks + 3280 fp16 local + 9816 int4 tier tokens): append the
+new token, decode attention with the fused window-mass accumulation, and on
+every 8th step the fused eviction (select, compact, re-rotate, quantise).
+Inputs are synthetic N(0,1) (seeded); the working set (~208 MB per step) is
+larger than the 126 MB L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs as torchrun ranks, one GPU each, every rank with its own batch of
+16 rows (weak scaling, no collective on the data path); the reported value
+is the sum over ranks of rows decoded per second, timed as the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, HQ, HKV, D, CTX = 16, 32, 8, 64, 32768
+WS, SINKS, LOCAL, BUDGET = 8, 4, 0.25, 0.40
+METRIC = "decode tokens/s (32k ctx, int4 tier, one attention layer)"
+UNIT = "tokens/s"
+
+
+def measured_hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def build_steady_cache(dev, seed):
+    """A layer cache at 32k context after its first eviction (steady state)."""
+    import numpy as np
+    import torch
+
+    from stickykv_b200 import WindowedCache, WindowedCacheConfig
+    from stickykv_b200.hooks import ATTN_IMPLEMENTATION  # noqa: F401
+
+    class MC:
+        num_attention_heads, num_key_value_heads, hidden_size, head_dim = HQ, HKV, HQ * D, D
+
+    class RoPE(torch.nn.Module):
+        def __init__(self, theta):
+            super().__init__()
+            self.inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.int64).float() / D))
+
+        def forward(self, x, pos):
+            f = pos[..., None].float() * self.inv.to(x.device)
+            emb = torch.cat([f, f], -1)
+            return emb.cos().to(x.dtype), emb.sin().to(x.dtype)
+
+    cfg = WindowedCacheConfig(window_size=WS, num_sink_tokens=SINKS, local_window_size=LOCAL,
+                              cache_budget=BUDGET, int4_tier=True)
+    cache = WindowedCache(cfg, CTX, MC(), torch.float16, RoPE(500000.0), num_layers=1, max_tokens=0)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    k = torch.randn(B, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
+    v = torch.randn(B, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
+    cache.update(k, v, 0)
+    del k, v
+    st = cache._states[0]
+    W = math.ceil((CTX - SINKS) / WS)
+    st.sides[st.cur].scores[:, :, :W] = torch.rand(B, HQ, W, device=dev, generator=g)
+    st.has_scores, st.W, st.next_window_id = True, W, W
+    # 9 decode steps: the 9th (generation step 8) runs the first eviction
+    q = torch.randn(B, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
+    for _ in range(WS + 1):
+        kn = torch.randn(B, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+        cache.update(kn, kn.clone(), 0)
+        cache.decode_attention(0, q, D ** -0.5)
+    torch.cuda.synchronize(dev)
+    return cache
+
+
+def algorithmic_bytes(cache):
+    """HBM bytes one decode-attention launch must move: every retained token's
+    K and V once (fp16 tokens 2*D*2 B; int4 tokens their page share) plus q and
+    out.  The window-mass write is not counted."""
+    from stickykv_b200 import _lib
+    st = cache._states[0]
+    n_fp = st.T - st.tier_pages * 8
+    per_int4 = _lib.page_bytes(D) / 8
+    return B * HKV * (n_fp * 2 * D * 2 + st.tier_pages * 8 * per_int4) + B * HQ * D * 2 * 2
+
+
+def run_ours(args, rank, world, dev):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    cache = build_steady_cache(dev, seed=1 + rank)
+    st = cache._states[0]
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    nq = 64
+    qs = torch.randn(nq, B, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
+    ks = torch.randn(nq, B, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+    vs = torch.randn(nq, B, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+    stream = torch.cuda.current_stream(dev)
+    scale = D ** -0.5
+
+    def step(i, ev=None):
+        j = i % nq
+        cache.update(ks[j], vs[j], 0)
+        if ev is not None:
+            ev[0].record(stream)
+        out = cache.decode_attention(0, qs[j], scale)
+        if ev is not None:
+            ev[1].record(stream)
+        return out
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    bytes_per_launch = algorithmic_bytes(cache)
+    attn_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+    step0 = cache._generation_step[0]
+    sampler = ClockSampler(dev.index if dev.index is not None else 0)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i, attn_events[i])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1)
+    attn_ms = [a.elapsed_time(b) for a, b in attn_events]
+    n_evict = sum(1 for s in range(step0, step0 + args.steps) if s > 0 and s % WS == 0)
+    # e2e: the same step through the public API with host buffers (pinned H2D
+    # of this step's q/k/v, D2H of the attention output) inside the timed region
+    hq = torch.randn(nq, B, HQ, 1, D, generator=torch.Generator().manual_seed(7), dtype=torch.float16).pin_memory()
+    hk = torch.randn(nq, B, HKV, 1, D, generator=torch.Generator().manual_seed(8), dtype=torch.float16).pin_memory()
+    hv = torch.randn(nq, B, HKV, 1, D, generator=torch.Generator().manual_seed(9), dtype=torch.float16).pin_memory()
+    hout = torch.empty(nq, B, 1, HQ, D, dtype=torch.float16).pin_memory()
+    dq = torch.empty(B, HQ, 1, D, device=dev, dtype=torch.float16)
+    dk = torch.empty(B, HKV, 1, D, device=dev, dtype=torch.float16)
+    dv = torch.empty(B, HKV, 1, D, device=dev, dtype=torch.float16)
+
+    def e2e_step(i):
+        j = i % nq
+        dq.copy_(hq[j], non_blocking=True)
+        dk.copy_(hk[j], non_blocking=True)
+        dv.copy_(hv[j], non_blocking=True)
+        cache.update(dk, dv, 0)
+        out = cache.decode_attention(0, dq, scale)
+        hout[j].copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = (dq.numel() + dk.numel() + dv.numel()) * 2
+    d2h = hout[0].numel() * 2
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, float(np.mean(attn_ms))], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, attn_avg = (float(x) for x in t.tolist())
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_hbm_peak()
+    achieved = bytes_per_launch / (attn_avg * 1e-3) / 1e9
+    launches_per_step = 1 + 2  # append + decode (+ merge)
+    gpu_launches = args.steps * launches_per_step + n_evict * 3
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("bytes_per_launch")
+        except (OSError, ValueError):
+            traffic = None
+    line = {
+        "metric": METRIC, "value": world * B * args.steps / (ms * 1e-3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 (int4 tier codes, fp32 accumulate)", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "decode-attention + eviction step of one layer, 32k context, int4 tier",
+                   "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
+                   "cache_budget": BUDGET, "window_size": WS, "sinks": SINKS, "local": LOCAL,
+                   "retained_tokens": st.T, "int4_tokens": st.tier_pages * 8,
+                   "evictions_in_timed_region": n_evict,
+                   "l2": "working set per step > 126 MB L2; no flush",
+                   "parallelism": f"{world} independent batch shards (weak scaling)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": "decode attention (split + merge) per layer-step",
+                     "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "avg_launch_us": attn_avg * 1e3},
+        "e2e": {"value": world * B * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    return line
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference's algorithm restated in numpy (oracle)
+# ------------------------------------------------------------------------------------------
+
+def cpu_reference_setup(rows: int):
+    """A reference-mode (all fp16) oracle cache for `rows` rows in the same
+    32k steady state (the reference has no int4 tier)."""
+    import numpy as np
+
+    from oracle import skv_oracle as O
+    inv = (1.0 / (500000.0 ** (np.arange(0, D, 2) / D))).astype(np.float32)
+    cos, sin = O.rope_tables(inv, CTX + 64)
+    r = O.resolve(WS, SINKS, LOCAL, BUDGET, CTX, HKV, D, 2, 0)
+    oc = O.OracleCache(r, "f16", cos, sin, tier=False)
+    rng = np.random.default_rng(0)
+    oc.update(rng.standard_normal((rows, HKV, CTX, D)).astype(np.float32),
+              rng.standard_normal((rows, HKV, CTX, D)).astype(np.float32), None)
+    W = math.ceil((CTX - SINKS) / WS)
+    oc.add_scores(rng.random((rows, HQ, W)).astype(np.float32))
+    for _ in range(WS + 1):
+        kn = rng.standard_normal((rows, HKV, 1, D)).astype(np.float32)
+        oc.update(kn, kn, None)
+    return oc, rng
+
+
+def cpu_step(oc, rng):
+    """One reference decode step: append (concatenate), eager attention with
+    the window scores of that step, accumulate, evict every 8th step."""
+    import numpy as np
+
+    from oracle import skv_oracle as O
+    rows = oc.k.shape[0]
+    kn = rng.standard_normal((rows, HKV, 1, D)).astype(np.float32)
+    scores = None
+    if getattr(oc, "_pending", None) is not None:
+        scores = oc._pending
+    oc.update(kn, kn, scores)
+    q = rng.standard_normal((rows, HQ, D)).astype(np.float32)
+    _, sc = O.eager_decode_attention(O.round_to(q, "f16"), oc.k, oc.v, D ** -0.5, SINKS, WS, "f16")
+    oc._pending = sc
+
+
+def cpu_baseline(seconds: float = 10.0, rows: int = 1):
+    import numpy as np
+    oc, rng = cpu_reference_setup(rows)
+    cpu_step(oc, rng)
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < WS:
+        cpu_step(oc, rng)
+        n += 1
+    dt = time.perf_counter() - t0
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        cores = max([i.get("num_threads", 1) for i in info] + [1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    return {"value": rows * n / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{rows} of {B} rows, {n} decode steps (incl. {n // WS} evictions), "
+                      f"all-fp16 retained cache of {oc.seq_length} tokens (reference has no int4 tier); "
+                      f"numpy restatement of the reference eager path, host cores = {os.cpu_count()}"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    oc, rng = cpu_reference_setup(1)
+    for _ in range(args.warmup):
+        cpu_step(oc, rng)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(oc, rng)
+    dt = time.perf_counter() - t0
+    value = 1 * args.steps / dt
+    try:
+        import threadpoolctl
+        cores = max([i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()] + [1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "decode-attention + eviction step of one layer, 32k context",
+                   "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
+                   "sample_rows": 1, "note": "reference CPU path (numpy restatement), all-fp16 tiers"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"1 of {B} rows per step, {args.steps} timed steps"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    try:
+        line = run_ours(args, rank, world, dev)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -84,8 +84,32 @@ class LayerState:
         self.device: Optional[torch.device] = None
         self.scores_cap = 0
         self.page_cap = 0
+        self.num_sink = 0
 
     # -- reference-compatible views --------------------------------------------
+    def _fp_view(self, which: str) -> Optional[Tensor]:
+        if not self.allocated:
+            return None
+        if self.tier_pages:
+            raise NotImplementedError(
+                "key_states/value_states of an int4-tier cache are not materialised; "
+                "read the fp store and the int4 pages instead")
+        side = self.sides[self.cur]
+        buf = side.k if which == "k" else side.v
+        s = min(self.num_sink, self.T)
+        s_pad = (self.num_sink + 7) // 8 * 8
+        rest = self.T - s
+        return torch.cat([buf[:, :, :s], buf[:, :, s_pad:s_pad + rest]], dim=2)
+
+    @property
+    def key_states(self) -> Optional[Tensor]:
+        """[B, Hkv, T, D] post-RoPE keys in logical order (a copy)."""
+        return self._fp_view("k")
+
+    @property
+    def value_states(self) -> Optional[Tensor]:
+        return self._fp_view("v")
+
     @property
     def seq_length(self) -> int:
         return self.T
@@ -230,6 +254,7 @@ class WindowedCache(_HFCacheBase):
         dev, dt = key.device, key.dtype
         cap_a, cap_b, wcap, max_T = self._caps(P)
         st.B, st.Hkv, st.Hq, st.D, st.dtype, st.device = B, Hkv, Hq, D, dt, dev
+        st.num_sink = self.resolved.num_sink_tokens
         st.scores_cap = wcap
         for side, cap in zip(st.sides, (cap_a, cap_b)):
             side.k = torch.empty(B, Hkv, cap, D, dtype=dt, device=dev)

@@ -1,0 +1,318 @@
+"""GPU parity: the native kernels (called through the C ABI by the drop-in
+cache) against the CPU oracle and the reference's golden vectors.
+
+Bit-exact: kept windows, original ids, position map, re-rotated fp keys,
+copied values, int4 codes/scales/page bytes.  Tolerance (max-abs, written per
+dtype in _helpers.OUT_TOL): attention outputs; window mass to 1e-4 relative.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import skv_oracle as O
+from tests._helpers import (OUT_TOL, TORCH_DT, fp_parts, make_cache, rand, rope_tables,
+                            tier_codes, to_np)
+
+pytestmark = pytest.mark.gpu
+G = os.path.join(os.path.dirname(__file__), "golden")
+DEV = "cuda"
+
+
+def setup_module(module):
+    assert torch.cuda.is_available(), "GPU tests need CUDA"
+    from stickykv_b200 import _lib
+    _lib.lib()
+
+
+# -- full cache drive against the reference's own run ------------------------------------
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_cache_drive_matches_reference_golden(dt):
+    z = np.load(os.path.join(G, f"cache_drive_{dt}.npz"))
+    B, Hkv, Hq, D, P, M = [int(x) for x in z["meta"]]
+    cache = make_cache(dt, B, Hkv, Hq, D, P, M, z["cos"], z["sin"], local=0.25, budget=0.5)
+    T = lambda a: torch.from_numpy(a).to(DEV, TORCH_DT[dt])
+    cache.update(T(z["k_0"]), T(z["v_0"]), 0)
+    for t in range(1, M + 1):
+        cache.update(T(z[f"k_{t}"]), T(z[f"v_{t}"]), 0,
+                     cache_kwargs={"window_scores": torch.from_numpy(z[f"s_{t - 1}"]).to(DEV)})
+        assert cache.get_seq_length(0) == int(z[f"len_{t}"])
+        np.testing.assert_array_equal(to_np(cache._states[0].original_window_ids), z[f"ids_{t}"])
+    st = cache._states[0]
+    np.testing.assert_array_equal(to_np(st.key_states), z["final_k"])
+    np.testing.assert_array_equal(to_np(st.value_states), z["final_v"])
+    np.testing.assert_allclose(to_np(st.window_scores), z["final_scores"], rtol=1e-6, atol=1e-7)
+    assert to_np(st.position_ids).tolist() == z["final_pos"].tolist()
+
+
+def test_divergent_eviction_kat_on_gpu():
+    # reference tests/test_windowed_cache.py:643-724 (head_dim 16: the smallest
+    # the kernels take; the KAT only reads which tokens survive)
+    D = 16
+    cos = np.ones((64, D), np.float32)
+    sin = np.zeros((64, D), np.float32)
+    rows = {}
+    for B in (2, 1):
+        cache = make_cache("f32", B, 2, 4, D, 8, 0, cos, sin, ws=1, s=0, local=1, budget=0.375)
+        assert cache.resolved.top_k_windows == 2
+        s0 = torch.zeros(B, 4, 8)
+        s0[0, :, [1, 3]] = 100.0
+        if B > 1:
+            s0[1, :, [5, 7]] = 100.0
+        keys = lambda n, a: torch.arange(a, a + n, dtype=torch.float32).view(1, 1, n, 1).expand(B, 2, n, D).contiguous().to(DEV)
+        k = keys(8, 0)
+        cache.update(k, k.clone(), 0, cache_kwargs={"window_scores": s0.to(DEV)})
+        for i, pos in enumerate((8, 9)):
+            k1 = keys(1, pos)
+            cache.update(k1, k1.clone(), 0, cache_kwargs={"window_scores": torch.zeros(B, 4, 9 + i, device=DEV)})
+        st = cache._states[0]
+        rows[B] = st
+        if B == 2:
+            assert to_np(st.original_window_ids).tolist() == [[1, 3, 9], [5, 7, 9]]
+            assert to_np(st.key_states[:, 0, :, 0]).tolist() == [[1.0, 3.0, 9.0], [5.0, 7.0, 9.0]]
+            assert to_np(st.position_ids).tolist() == [[0, 1, 2], [0, 1, 2]]
+    np.testing.assert_array_equal(to_np(rows[1].key_states[0]), to_np(rows[2].key_states[0]))
+
+
+# -- decode attention ---------------------------------------------------------------------
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_decode_matches_reference_eager_golden(dt):
+    z = np.load(os.path.join(G, f"eager_decode_{dt}.npz"))
+    B, Hq, D = z["q"].shape
+    Hkv, S = z["k"].shape[1], z["k"].shape[2]
+    cos, sin = rope_tables(1e4, D, 256)
+    cache = make_cache(dt, B, Hkv, Hq, D, S, 1, cos, sin)
+    T = lambda a: torch.from_numpy(a).to(DEV, TORCH_DT[dt])
+    cache.update(T(z["k"]), T(z["v"]), 0)
+    st = cache._states[0]
+    st.has_scores, st.W = True, 0
+    out = cache.decode_attention(0, T(z["q"])[:, :, None, :], D ** -0.5)
+    np.testing.assert_allclose(to_np(out[:, 0]), z["out"], atol=OUT_TOL[dt], rtol=0)
+    np.testing.assert_allclose(to_np(st.window_scores), z["scores"], atol=OUT_TOL[dt], rtol=0)
+
+
+@pytest.mark.parametrize("dt,D,G,S", [("f32", 64, 2, 300), ("f16", 64, 4, 1000), ("bf16", 128, 4, 777),
+                                      ("f16", 128, 8, 64), ("bf16", 64, 1, 2049), ("f16", 32, 4, 5000)])
+def test_decode_matches_oracle(dt, D, G, S):
+    g = torch.Generator().manual_seed(S + D)
+    B, Hkv = 3, 2
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, S + 64)
+    cache = make_cache(dt, B, Hkv, Hq, D, S, 1, cos, sin)
+    k, v = rand((B, Hkv, S, D), dt, g), rand((B, Hkv, S, D), dt, g)
+    q = rand((B, Hq, D), dt, g, scale=2.0)
+    cache.update(k.to(DEV), v.to(DEV), 0)
+    st = cache._states[0]
+    before = to_np(st.sides[st.cur].scores[:, :, : math.ceil((S - 4) / 8)])
+    out = cache.decode_attention(0, q.to(DEV)[:, :, None, :], D ** -0.5)
+    ref_out, ref_mass = O.tiered_decode_attention(
+        to_np(q), to_np(k)[:, :, :4], to_np(v)[:, :, :4], None, None, to_np(k)[:, :, 4:],
+        to_np(v)[:, :, 4:], 4, 8, D ** -0.5)
+    np.testing.assert_allclose(to_np(out[:, 0]), ref_out, atol=OUT_TOL[dt], rtol=0)
+    mass = to_np(st.window_scores) - before
+    np.testing.assert_allclose(mass, ref_mass, rtol=1e-4, atol=1e-6)
+    # the mass of all windows plus the sinks is the whole softmax
+    assert np.all(mass.sum(-1) <= 1 + 1e-4)
+
+
+# -- int4 pages ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("dt,D", [("f16", 64), ("bf16", 128), ("f32", 32)])
+def test_pack_pages_bit_exact(dt, D):
+    import ctypes
+    from stickykv_b200 import _lib
+    g = torch.Generator().manual_seed(7 + D)
+    n_pages, s = 37, 4
+    first = s + 8 * 11
+    cos, sin = rope_tables(5e5, D, first + 8 * n_pages + 8)
+    k = rand((n_pages * 8, D), dt, g, scale=3.0)
+    v = rand((n_pages * 8, D), dt, g)
+    k[5, :32] = 1.25  # a constant group: scale 0
+    out = torch.zeros(n_pages, _lib.page_bytes(D), dtype=torch.uint8, device=DEV)
+    d = _lib.LayerDesc()
+    d.head_dim, d.kv_dtype = D, {"f32": 0, "f16": 1, "bf16": 2}[dt]
+    ct = torch.from_numpy(cos[:, : D // 2].copy()).to(DEV)
+    stt = torch.from_numpy(sin[:, : D // 2].copy()).to(DEV)
+    d.rope_cos, d.rope_sin, d.rope_positions = ct.data_ptr(), stt.data_ptr(), cos.shape[0]
+    kd, vd = k.to(DEV), v.to(DEV)
+    _lib.check(_lib.lib().skv_pack_pages(ctypes.byref(d), kd.data_ptr(), vd.data_ptr(), first, n_pages,
+                                         out.data_ptr(), torch.cuda.current_stream().cuda_stream),
+               "skv_pack_pages")
+    got = out.cpu().numpy()
+    kn, vn = to_np(k), to_np(v)
+    for pg in range(n_pages):
+        sl = slice(pg * 8, pg * 8 + 8)
+        kf = O.to_page_frame(kn[sl], np.arange(first + 8 * pg, first + 8 * pg + 8), cos, sin, s)
+        kc, ks, kz = O.quantize_group32(kf)
+        vc, vs, vz = O.quantize_group32(vn[sl])
+        np.testing.assert_array_equal(got[pg], O.pack_page(kc, ks, kz, vc, vs, vz), err_msg=f"page {pg}")
+
+
+# -- eviction -----------------------------------------------------------------------------
+
+def _drive_pair(dt, tier, B=3, Hkv=2, G=4, D=64, P=203, steps=30, seed=0, budget=0.4, local=0.25):
+    """Drive the GPU cache and the oracle cache with identical K/V; scores
+    come from the GPU decode kernel each step and are fed to both."""
+    g = torch.Generator().manual_seed(seed)
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, P + steps + 64)
+    cache = make_cache(dt, B, Hkv, Hq, D, P, steps, cos, sin, budget=budget, local=local, tier=tier)
+    r = cache.resolved
+    oc = O.OracleCache(O.resolve(8, 4, local, budget, P, Hkv, D, O.DTYPE_SIZES[dt], steps), dt, cos, sin,
+                       tier=tier)
+    k, v = rand((B, Hkv, P, D), dt, g), rand((B, Hkv, P, D), dt, g)
+    cache.update(k.to(DEV), v.to(DEV), 0)
+    oc.update(to_np(k), to_np(v), None)
+    scores = O.compute_window_scores(np.random.default_rng(seed).random((B, Hq, 1, P)).astype(np.float32), 4, 8)
+    st = cache._states[0]
+    st.sides[st.cur].scores[:, :, : scores.shape[-1]] = torch.from_numpy(scores).to(DEV)
+    st.has_scores, st.W, st.next_window_id = True, scores.shape[-1], scores.shape[-1]
+    oc.add_scores(scores)
+    evictions = 0
+    for t in range(steps):
+        k1, v1 = rand((B, Hkv, 1, D), dt, g), rand((B, Hkv, 1, D), dt, g)
+        n_before = oc.seq_length
+        cache.update(k1.to(DEV), v1.to(DEV), 0)
+        evicted = oc.update(to_np(k1), to_np(v1), None)
+        evictions += evicted
+        assert cache.get_seq_length(0) == oc.seq_length
+        if evicted:
+            yield "evict", cache, oc
+        q = rand((B, Hq, D), dt, g, scale=2.0)
+        before = to_np(st.sides[st.cur].scores[:, :, : st.W]) if st.W else None
+        out = cache.decode_attention(0, q.to(DEV)[:, :, None, :], D ** -0.5)
+        ref_out, ref_mass = oc.decode_attention(to_np(q), D ** -0.5)
+        yield "decode", (out, ref_out, t)
+        # feed the GPU's step scores to the oracle (identical inputs for selection)
+        acc = to_np(st.sides[st.cur].scores[:, :, : st.W])
+        step_scores = acc.copy()
+        if before is not None:
+            step_scores[:, :, : before.shape[-1]] -= before
+        oc.window_scores = None if oc.window_scores is None else oc.window_scores
+        W_new = acc.shape[-1]
+        W_old = oc.window_scores.shape[-1]
+        if W_new > W_old:
+            oc.add_scores(np.zeros(acc.shape[:2] + (W_new,), np.float32))
+        oc.window_scores = acc.copy()
+    assert evictions == (steps - 1) // 8
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16", "f16"])
+def test_reference_mode_eviction_bit_exact(dt):
+    for kind, *rest in _drive_pair(dt, tier=False):
+        if kind == "evict":
+            cache, oc = rest
+            st = cache._states[0]
+            np.testing.assert_array_equal(to_np(st.key_states), oc.k)
+            np.testing.assert_array_equal(to_np(st.value_states), oc.v)
+            np.testing.assert_array_equal(to_np(st.window_scores), oc.window_scores)
+            np.testing.assert_array_equal(to_np(st.original_window_ids), oc.original_window_ids)
+        else:
+            out, ref_out, t = rest[0]
+            np.testing.assert_allclose(to_np(out[:, 0]), ref_out, atol=OUT_TOL[dt], rtol=0)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_int4_tier_eviction_and_decode(dt):
+    n_checked = 0
+    for kind, *rest in _drive_pair(dt, tier=True, P=403, steps=34, seed=3):
+        if kind == "evict":
+            cache, oc = rest
+            st = cache._states[0]
+            assert st.tier_pages * 8 == oc.n_tier_tokens
+            sk, sv, rk, rv = fp_parts(cache)
+            s = min(4, oc.k.shape[2])
+            np.testing.assert_array_equal(sk, oc.k[:, :, :s])
+            np.testing.assert_array_equal(sv, oc.v[:, :, :s])
+            np.testing.assert_array_equal(rk, oc.k[:, :, s:])
+            np.testing.assert_array_equal(rv, oc.v[:, :, s:])
+            for a, b in zip(tier_codes(cache), oc.tier_codes):
+                np.testing.assert_array_equal(a, b)
+            np.testing.assert_array_equal(to_np(st.window_scores), oc.window_scores)
+            np.testing.assert_array_equal(to_np(st.original_window_ids), oc.original_window_ids)
+            n_checked += 1
+        else:
+            out, ref_out, t = rest[0]
+            np.testing.assert_allclose(to_np(out[:, 0]), ref_out, atol=OUT_TOL[dt], rtol=0)
+    assert n_checked == 4
+
+
+# -- prefill ------------------------------------------------------------------------------
+
+def test_prefill_scores_match_reference_golden():
+    z = np.load(os.path.join(G, "prefill_scores.npz"))
+    B, Hq, T, D = z["q"].shape
+    Hkv = z["k"].shape[1]
+    cos, sin = rope_tables(1e4, D, 128)
+    cache = make_cache("f32", B, Hkv, Hq, D, T, 1, cos, sin)
+    k = torch.from_numpy(z["k"]).to(DEV)
+    v = torch.randn(B, Hkv, T, D).to(DEV)
+    q = torch.from_numpy(z["q"]).to(DEV)
+    cache.update(k, v, 0)
+    out = cache.prefill_attention(0, q, k, v, D ** -0.5)
+    np.testing.assert_allclose(to_np(cache._states[0].window_scores), z["scores"], rtol=1e-5, atol=2e-5)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q, k.repeat_interleave(Hq // Hkv, 1), v.repeat_interleave(Hq // Hkv, 1), is_causal=True)
+    np.testing.assert_allclose(to_np(out), to_np(ref.transpose(1, 2)), atol=1e-5)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_prefill_matches_oracle(dt):
+    g = torch.Generator().manual_seed(5)
+    B, Hkv, G, D, T = 2, 2, 4, 64, 333
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, 400)
+    cache = make_cache(dt, B, Hkv, Hq, D, T, 1, cos, sin)
+    q, k, v = rand((B, Hq, T, D), dt, g), rand((B, Hkv, T, D), dt, g), rand((B, Hkv, T, D), dt, g)
+    cache.update(k.to(DEV), v.to(DEV), 0)
+    out = cache.prefill_attention(0, q.to(DEV), k.to(DEV), v.to(DEV), D ** -0.5)
+    ref = O.prefill_window_scores(to_np(q), to_np(k), D ** -0.5, 4, 8)
+    np.testing.assert_allclose(to_np(cache._states[0].window_scores), ref, rtol=2e-4, atol=1e-4)
+    qd, kd, vd = (x.to(DEV).float() for x in (q, k, v))
+    sd = torch.nn.functional.scaled_dot_product_attention(
+        qd, kd.repeat_interleave(G, 1), vd.repeat_interleave(G, 1), is_causal=True)
+    np.testing.assert_allclose(to_np(out), to_np(sd.transpose(1, 2)), atol=OUT_TOL[dt])
+
+
+# -- full-size properties ----------------------------------------------------------------
+
+def test_cfg3_scale_eviction_selection_and_codes():
+    """16 rows x 8 kv heads x 16384 tokens (bf16): the kept windows equal the
+    oracle's selection on the same scores; spot rows' int4 codes are bit-exact;
+    every row keeps 6544 tokens."""
+    dt, B, Hkv, Hq, D, P = "bf16", 16, 8, 32, 64, 16384
+    g = torch.Generator().manual_seed(2)
+    cos, sin = rope_tables(5e5, D, P + 64)
+    cache = make_cache(dt, B, Hkv, Hq, D, P, 0, cos, sin, tier=True)
+    k = rand((B, Hkv, P, D), dt, g).to(DEV)
+    v = rand((B, Hkv, P, D), dt, g).to(DEV)
+    cache.update(k, v, 0)
+    st = cache._states[0]
+    W = math.ceil((P - 4) / 8)
+    scores = torch.rand(B, Hq, W, generator=g)
+    st.sides[st.cur].scores[:, :, :W] = scores.to(DEV)
+    st.has_scores, st.W, st.next_window_id = True, W, W
+    for t in range(9):
+        cache.update(k[:, :, :1].clone(), v[:, :, :1].clone(), 0)
+    r = cache.resolved
+    assert (r.top_k_windows, r.local_tokens) == (613, 1640)
+    ret = O.retain_window_indices(to_np(scores), r.top_k_windows, r.local_tokens // 8)
+    # 16393 tokens at the eviction: the 9 appended tokens past window 2047 are
+    # not covered by the scores and drop, as in the reference (6544 + 4)
+    assert cache.get_seq_length(0) == O.expand_to_token_indices(ret, 4, 8, P + 9).shape[1] == 6548
+    np.testing.assert_array_equal(to_np(st.original_window_ids), ret)
+    codes = tier_codes(cache, rows=2)
+    kn = to_np(k[:2, :, :])
+    for b in range(2):
+        for j in (0, 100, 612):
+            w = int(ret[b, j])
+            pos = 4 + 8 * w + np.arange(8)
+            kf = O.to_page_frame(kn[b][:, pos], np.broadcast_to(pos, (Hkv, 8)), cos, sin, 4)
+            kc, ks, kz = O.quantize_group32(kf)
+            np.testing.assert_array_equal(codes[0][b, :, j * 8:(j + 1) * 8], kc)
+            np.testing.assert_array_equal(codes[1][b, :, j * 8:(j + 1) * 8], ks)
