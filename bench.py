@@ -84,7 +84,7 @@ class ClockSampler:
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v})
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
 

@@ -32,7 +32,9 @@ class TableRoPE(torch.nn.Module):
         self.sin = torch.from_numpy(np.ascontiguousarray(sin, np.float32))
 
     def forward(self, x, position_ids):
-        pos = position_ids.to("cpu").long()
+        # the cache asks for headroom past the last real position; rows past
+        # the table repeat its last row and are never read for real tokens
+        pos = position_ids.to("cpu").long().clamp(max=self.cos.shape[0] - 1)
         c = self.cos[pos].to(x.device, x.dtype)
         s = self.sin[pos].to(x.device, x.dtype)
         return c, s
