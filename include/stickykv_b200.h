@@ -161,6 +161,27 @@ int skv_decode_attention(const skv_layer_desc* layer, int32_t seq_len, int32_t t
                          size_t workspace_bytes, void* stream);
 
 /*
+ * skv_decode_attention without a workspace argument (no counterpart in the
+ * reference).  For callers that cannot allocate device memory: a binding from
+ * a language without a CUDA allocator, a service that forbids allocation on
+ * its decode path, or a plugin that only receives tensors it did not create.
+ * The scratch is a fixed array of SKV_NOALLOC_SCRATCH_BYTES (16 MiB) inside
+ * this library, reserved on every GPU that loads it until the process exits;
+ * a request whose scratch (skv_decode_workspace_size) is larger returns
+ * SKV_ERR_CAPACITY.  The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture.  No cudaMalloc/cudaFree or other allocation happens.  All calls
+ * share the one array: calls whose kernels overlap on the GPU (different
+ * streams, or the same layer from two threads) race on it and must be
+ * serialised by the caller.
+ */
+#define SKV_NOALLOC_SCRATCH_BYTES (16u << 20)
+int skv_decode_attention_noalloc(const skv_layer_desc* layer, int32_t seq_len, int32_t tier_pages,
+                                 const void* q, int64_t q_stride_b, int64_t q_stride_h, void* out,
+                                 int64_t out_stride_b, int64_t out_stride_h, float scaling,
+                                 float* window_scores, int32_t scores_capacity, void* stream);
+
+/*
  * Eviction: select the kept windows per row from args->scores_src (head
  * mean, top-k over the evictable prefix, lowest index wins ties,
  * chronological order), compact src into dst (dst has its own fp buffers and
