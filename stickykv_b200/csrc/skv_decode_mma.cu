@@ -30,6 +30,8 @@
 // and adds the normalised window mass to the fp32 score accumulator.
 #include <float.h>
 
+#include <type_traits>
+
 #include "skv_common.cuh"
 
 namespace skv {
@@ -43,7 +45,7 @@ constexpr int kMaxUnitsPerSplit = 2 * kWarps * kMaxTilesPerWarp;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D> struct Cfg {
-  static constexpr int kStages = D == 64 ? 4 : 3;
+  static constexpr int kStages = 3;
   static constexpr int kHalfBytes = 32 * D;           // one unit: fp K+V rows, or int4 page + cos/sin
   static constexpr int kPageBytes = page_bytes(D);
   static constexpr int kCPR = D / 8;                  // 16-byte chunks per fp row
@@ -212,7 +214,9 @@ __device__ __forceinline__ void issue_unit(const MmaParams& p, const Unit& x, in
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_constant__ MmaParams p) {
   using C = Cfg<D>;
-  using O = Op<T>;
+  using O = Op<T>;        // fp units: the KV dtype
+  using H = Op<__half>;   // int4 pages: fp16
+  constexpr bool kBF = !std::is_same<T, __half>::value;
   constexpr int KB = C::kKB, NW = C::kNW;
   extern __shared__ __align__(128) unsigned char smem[];
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -277,6 +281,11 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     __syncwarp();
     const int ua = u0 + 2 * (warp + kWarps * i);
     const Unit UA = unit_info(p, ua, u1, tbl, j0), UB = unit_info(p, ua + 1, u1, tbl, j0);
+    // operand class of each unit's MMAs: 0 = KV dtype (fp units), 1 = fp16
+    // (int4 pages, whose fp16 scale/zero make fp16 the exact dequant type);
+    // a missing unit follows the other one
+    const int clsA = (UA.kind == 2 || (UA.kind == 0 && UB.kind == 2)) ? 1 : 0;
+    const int clsB = (UB.kind == 2 || (UB.kind == 0 && UA.kind == 2)) ? 1 : 0;
     unsigned char* st = ring + (size_t)(i % C::kStages) * C::kStageBytes;
     const uint32_t st_s = smem_u32(st);
 
@@ -300,10 +309,10 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
             xr[e] = fmaf(x, cc[e], y * ss[e]);
             yr[e] = fmaf(y, cc[e], -x * ss[e]);
           }
-          qB[kb][0] = O::pack(xr[0], xr[1]);
-          qB[kb][1] = O::pack(xr[2], xr[3]);
-          qB[kb + KB / 2][0] = O::pack(yr[0], yr[1]);
-          qB[kb + KB / 2][1] = O::pack(yr[2], yr[3]);
+          qB[kb][0] = H::pack(xr[0], xr[1]);
+          qB[kb][1] = H::pack(xr[2], xr[3]);
+          qB[kb + KB / 2][0] = H::pack(yr[0], yr[1]);
+          qB[kb + KB / 2][1] = H::pack(yr[2], yr[3]);
         }
       } else {
 #pragma unroll
@@ -331,10 +340,10 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
 #pragma unroll
           for (int kb = 0; kb < KB; ++kb) {
             const uint32_t szw = sz[kb >> 1];
-            const uint32_t s2 = O::from_f16x2(__byte_perm(szw, szw, 0x1010));
-            const uint32_t z2 = O::from_f16x2(__byte_perm(szw, szw, 0x3232));
-            ka[h][kb][0] = O::fma2(O::codes(w[kb >> 1], 2 * (kb & 1)), s2, z2);
-            ka[h][kb][1] = O::fma2(O::codes(w[kb >> 1], 2 * (kb & 1) + 1), s2, z2);
+            const uint32_t s2 = __byte_perm(szw, szw, 0x1010);
+            const uint32_t z2 = __byte_perm(szw, szw, 0x3232);
+            ka[h][kb][0] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1)), s2, z2);
+            ka[h][kb][1] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1) + 1), s2, z2);
           }
         } else {
           const int r = lane & 7, sel = (lane >> 3) & 1;
@@ -343,9 +352,27 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
             ldsm_x2(ka[h][kb][0], ka[h][kb][1], hb + r * (2 * D) + (((2 * kb + sel) ^ r) * 16));
         }
       }
+      if (!kBF || clsA == clsB) {
 #pragma unroll
-      for (int kb = 0; kb < KB; ++kb)
-        O::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (kBF && clsA == 1)
+            H::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+          else
+            O::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+        }
+      } else {
+        // tier boundary in a bf16 cache: one MMA per operand type, the other
+        // unit's rows and the other columns' query zeroed
+        const bool colF16 = ((g >> 2) ? clsB : clsA) == 1;
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb) {
+          const uint32_t n0 = clsA == 0 ? 0xFFFFFFFFu : 0u, n1 = clsB == 0 ? 0xFFFFFFFFu : 0u;
+          O::mma(sacc, ka[0][kb][0] & n0, ka[1][kb][0] & n1, ka[0][kb][1] & n0, ka[1][kb][1] & n1,
+                 colF16 ? 0u : qB[kb][0], colF16 ? 0u : qB[kb][1]);
+          H::mma(sacc, ka[0][kb][0] & ~n0, ka[1][kb][0] & ~n1, ka[0][kb][1] & ~n0, ka[1][kb][1] & ~n1,
+                 colF16 ? qB[kb][0] : 0u, colF16 ? qB[kb][1] : 0u);
+        }
+      }
     }
 
     // ---- online softmax (log2 domain) for this thread's two heads ----
@@ -390,8 +417,10 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     }
 
     // ---- O^T += V^T P ----
-    const uint32_t px = O::pack(my_unit == 0 ? pr[0] : 0.f, my_unit == 0 ? pr[1] : 0.f);
-    const uint32_t py = O::pack(my_unit == 1 ? pr[0] : 0.f, my_unit == 1 ? pr[1] : 0.f);
+    const float xa = my_unit == 0 ? pr[0] : 0.f, xb = my_unit == 0 ? pr[1] : 0.f;
+    const float ya = my_unit == 1 ? pr[0] : 0.f, yb = my_unit == 1 ? pr[1] : 0.f;
+    const uint32_t px = (kBF && clsA == 1) ? H::pack(xa, xb) : O::pack(xa, xb);
+    const uint32_t py = (kBF && clsB == 1) ? H::pack(ya, yb) : O::pack(ya, yb);
     const uint32_t pb0 = movm_t(px), pb1 = movm_t(py);
     {
       uint32_t va[2][KB][2];  // [unit][mb][d rows g / g+8]
@@ -407,9 +436,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
 #pragma unroll
           for (int mb = 0; mb < KB; ++mb) {
             const uint2 sz = reinterpret_cast<const uint2*>(pg + page_v_scales_off(D))[t * NW + (mb >> 1)];
-            const uint32_t s2 = O::from_f16x2(sz.x), z2 = O::from_f16x2(sz.y);
-            va[h][mb][0] = O::fma2(O::codes(w[mb >> 1], 2 * (mb & 1)), s2, z2);
-            va[h][mb][1] = O::fma2(O::codes(w[mb >> 1], 2 * (mb & 1) + 1), s2, z2);
+            va[h][mb][0] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1)), sz.x, sz.y);
+            va[h][mb][1] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1) + 1), sz.x, sz.y);
           }
         } else {
           const int r = lane & 7, sel = (lane >> 3) & 1;
@@ -423,9 +451,24 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
           }
         }
       }
+      if (!kBF || clsA == clsB) {
 #pragma unroll
-      for (int mb = 0; mb < KB; ++mb)
-        O::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
+        for (int mb = 0; mb < KB; ++mb) {
+          if (kBF && clsA == 1)
+            H::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
+          else
+            O::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
+        }
+      } else {
+        const uint32_t n0 = clsA == 0 ? 0xFFFFFFFFu : 0u, n1 = clsB == 0 ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+        for (int mb = 0; mb < KB; ++mb) {
+          O::mma(o[mb], va[0][mb][0] & n0, va[0][mb][1] & n0, va[1][mb][0] & n1, va[1][mb][1] & n1,
+                 pb0 & n0, pb1 & n1);
+          H::mma(o[mb], va[0][mb][0] & ~n0, va[0][mb][1] & ~n0, va[1][mb][0] & ~n1, va[1][mb][1] & ~n1,
+                 pb0 & ~n0, pb1 & ~n1);
+        }
+      }
     }
     __syncwarp();
   }
@@ -554,7 +597,7 @@ void plan_splits(MmaParams& p) {
   const double c_fp = 32.0 * D, c_i4 = (double)(C::kPageBytes + 4 * D);
   const double total = p.NS * c_fp + p.n_tp * c_i4 + (p.U - p.NS - p.n_tp) * c_fp;
   const int units = p.B * p.Hkv;
-  const int resident = D == 64 ? 3 : 2;
+  const int resident = D == 64 ? 4 : 2;
   int n = ceil_div(2 * 148 * resident, units > 0 ? units : 1);
   n = max(n, ceil_div(p.U, kMaxUnitsPerSplit));
   n = min(n, kMaxSplits);
