@@ -89,7 +89,7 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
 
 
-def build_steady_cache(dev, seed):
+def build_steady_cache(dev, seed, tier=True):
     """A layer cache at 32k context after its first eviction (steady state)."""
     import numpy as np
     import torch
@@ -111,7 +111,7 @@ def build_steady_cache(dev, seed):
             return emb.cos().to(x.dtype), emb.sin().to(x.dtype)
 
     cfg = WindowedCacheConfig(window_size=WS, num_sink_tokens=SINKS, local_window_size=LOCAL,
-                              cache_budget=BUDGET, int4_tier=True)
+                              cache_budget=BUDGET, int4_tier=tier)
     cache = WindowedCache(cfg, CTX, MC(), torch.float16, RoPE(500000.0), num_layers=1, max_tokens=0)
     g = torch.Generator(device=dev).manual_seed(seed)
     k = torch.randn(B, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
@@ -148,7 +148,7 @@ def run_ours(args, rank, world, dev):
     import torch
     import torch.distributed as dist
 
-    cache = build_steady_cache(dev, seed=1 + rank)
+    cache = build_steady_cache(dev, seed=1 + rank, tier=not args.no_tier)
     st = cache._states[0]
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     nq = 64
@@ -249,7 +249,8 @@ def run_ours(args, rank, world, dev):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 (int4 tier codes, fp32 accumulate)", "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "decode-attention + eviction step of one layer, 32k context, int4 tier",
+        "config": {"workload": "decode-attention + eviction step of one layer, 32k context, "
+                               + ("all-fp16 retained cache" if args.no_tier else "int4 tier"),
                    "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
                    "cache_budget": BUDGET, "window_size": WS, "sinks": SINKS, "local": LOCAL,
                    "retained_tokens": st.T, "int4_tokens": st.tier_pages * 8,
@@ -373,6 +374,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tier", action="store_true",
+                    help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -73,7 +73,7 @@ struct MmaParams {
   float* mass;     // [B][Hq][W]: window mass relative to its split's max
   int64_t q_sb, q_sh, o_sb, o_sh;
   int B, Hkv, cap, page_cap, scores_cap, n_split;
-  int s, s_eff, s_pad, NS, n_tp, rest, U, W;
+  int s, s_eff, s_pad, NS, n_tp, rest, U, W, rope_rows;
   float scale_log2;
   int bnd[kMaxSplits + 1];
 };
@@ -149,102 +149,118 @@ __device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, uint32_t a
                : "=r"(r0), "=r"(r1)
                : "r"(addr));
 }
+__device__ __forceinline__ void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
   return y;
 }
 
-// kind: 0 none, 1 fp, 2 int4 page
-struct Unit {
-  int kind, valid, window, src, P;
+// Unit kinds: 0 none, 1 fp (KV dtype rows in the fp store), 2 int4 page.
+struct Regions {
+  int NS, TB, U, u1;  // sinks [0,NS), tier [NS,TB), fp rest [TB,U); split end u1
+  __device__ __forceinline__ int kind(int u) const { return u >= u1 ? 0 : ((u >= NS && u < TB) ? 2 : 1); }
 };
 
-__device__ __forceinline__ Unit unit_info(const MmaParams& p, int u, int u_end, const int* tbl, int tbl0) {
-  Unit x{0, 0, -1, 0, 0};
-  if (u >= u_end) return x;
-  if (u < p.NS) {
-    x.kind = 1;
-    x.src = 8 * u;
-    x.valid = min(8, p.s_eff - 8 * u);
-  } else if (u < p.NS + p.n_tp) {
-    const int j = u - p.NS;
-    x.kind = 2;
-    x.src = tbl[j - tbl0];
-    x.P = p.s + 8 * j;
-    x.valid = 8;
-    x.window = j;
-  } else {
-    const int r = u - p.NS - p.n_tp;
-    x.kind = 1;
-    x.src = p.s_pad + 8 * r;
-    x.valid = min(8, p.rest - 8 * r);
-    x.window = p.n_tp + r;
-  }
-  return x;
+__device__ __forceinline__ int fp_slot0(const MmaParams& p, const Regions& R, int u) {
+  return u < R.NS ? 8 * u : p.s_pad + 8 * (u - R.TB);
+}
+__device__ __forceinline__ int fp_valid(const MmaParams& p, const Regions& R, int u) {
+  return u < R.NS ? min(8, p.s_eff - 8 * u) : min(8, p.rest - 8 * (u - R.TB));
 }
 
 template <typename T, int D>
-__device__ __forceinline__ void issue_unit(const MmaParams& p, const Unit& x, int b, int kh,
-                                           unsigned char* half, int lane) {
-  using C = Cfg<D>;
-  if (x.kind == 1) {
-    const T* kr = (const T*)p.k_fp + (((int64_t)b * p.Hkv + kh) * p.cap + x.src) * D;
-    const T* vr = (const T*)p.v_fp + (((int64_t)b * p.Hkv + kh) * p.cap + x.src) * D;
-    const uint32_t base = smem_u32(half);
-#pragma unroll
-    for (int idx = lane; idx < 8 * C::kCPR; idx += 32) {
-      const int r = idx / C::kCPR, c = idx % C::kCPR;
-      const uint32_t off = r * (2 * D) + ((c ^ (r & 7)) * 16);
-      cp_async16(base + off, kr + r * D + c * 8);
-      cp_async16(base + 16 * D + off, vr + r * D + c * 8);
-    }
-  } else if (x.kind == 2) {
-    const uint8_t* pg = p.pages + (((int64_t)b * p.Hkv + kh) * p.page_cap + x.src) * C::kPageBytes;
-    const uint32_t base = smem_u32(half);
-    for (int idx = lane; idx < C::kPageBytes / 16; idx += 32) cp_async16(base + idx * 16, pg + idx * 16);
-    const float* cs = p.cos + (int64_t)x.P * (D / 2);
-    const float* sn = p.sin + (int64_t)x.P * (D / 2);
-    for (int idx = lane; idx < D / 8; idx += 32) cp_async16(base + C::kPageBytes + idx * 16, cs + idx * 4);
-    for (int idx = lane; idx < D / 8; idx += 32)
-      cp_async16(base + C::kPageBytes + 2 * D + idx * 16, sn + idx * 4);
-  }
-}
-
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_constant__ MmaParams p) {
+__global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(const __grid_constant__ MmaParams p) {
   using C = Cfg<D>;
   using O = Op<T>;        // fp units: the KV dtype
-  using H = Op<__half>;   // int4 pages: fp16
+  using H = Op<__half>;   // int4 pages: fp16 (their scale/zero are fp16)
   constexpr bool kBF = !std::is_same<T, __half>::value;
   constexpr int KB = C::kKB, NW = C::kNW;
+  constexpr int FP_IT = 8 * C::kCPR / 32;                 // cp.async per lane per fp tensor
+  constexpr int PG_CH = C::kPageBytes / 16;               // 16-byte chunks per page
+  constexpr int PG_IT = (PG_CH + 31) / 32;
+  constexpr float kThresh = 8.f;                          // lazy rescale margin (log2 domain)
   extern __shared__ __align__(128) unsigned char smem[];
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int u0 = p.bnd[split], u1 = p.bnd[split + 1];
   const int n_tiles = (u1 - u0 + 1) >> 1;
+  const Regions R{p.NS, p.NS + p.n_tp, p.U, u1};
 
   unsigned char* ring = smem + (size_t)warp * C::kStages * C::kStageBytes;
   float* mass_s = reinterpret_cast<float*>(smem + C::kRingBytes) + warp * kMaxTilesPerWarp * 12;
   int* tbl = reinterpret_cast<int*>(smem + C::kRingBytes + C::kMassBytes);
 
-  // page-table slice of this split
   const int j0 = max(0, u0 - p.NS), j1 = min(p.n_tp, max(0, u1 - p.NS));
   for (int j = j0 + threadIdx.x; j < j1; j += kThreads) tbl[j - j0] = p.table[(int64_t)b * p.page_cap + j];
   __syncthreads();
 
+  // per-lane copy offsets (constant for the whole kernel)
+  uint32_t fp_soff[FP_IT];
+  int fp_goff[FP_IT];
+#pragma unroll
+  for (int j = 0; j < FP_IT; ++j) {
+    const int idx = lane + 32 * j, r = idx / C::kCPR, c = idx % C::kCPR;
+    fp_soff[j] = r * (2 * D) + ((c ^ (r & 7)) * 16);
+    fp_goff[j] = r * D + c * 8;
+  }
+  const int64_t kv_row = ((int64_t)b * p.Hkv + kh) * p.cap * D;
+  const int64_t pg_row = ((int64_t)b * p.Hkv + kh) * p.page_cap;
+  const T* kfp = (const T*)p.k_fp + kv_row;
+  const T* vfp = (const T*)p.v_fp + kv_row;
+
+  auto issue_unit = [&](int u, unsigned char* half) {
+    const int kd = R.kind(u);
+    const uint32_t hs = smem_u32(half);
+    if (kd == 1) {
+      const int64_t off = (int64_t)fp_slot0(p, R, u) * D;
+#pragma unroll
+      for (int j = 0; j < FP_IT; ++j) {
+        cp_async16(hs + fp_soff[j], kfp + off + fp_goff[j]);
+        cp_async16(hs + 16 * D + fp_soff[j], vfp + off + fp_goff[j]);
+      }
+    } else if (kd == 2) {
+      const uint8_t* pg = p.pages + (pg_row + tbl[u - p.NS - j0]) * C::kPageBytes;
+#pragma unroll
+      for (int j = 0; j < PG_IT; ++j) {
+        const int idx = lane + 32 * j;
+        if (idx < PG_CH) cp_async16(hs + idx * 16, pg + idx * 16);
+      }
+    }
+  };
+
   // query of head (g & 3) in B-fragment order: d = 16kb + 2t + {0,1,8,9}
   const T* qp = (const T*)p.q + b * p.q_sb + (kh * 4 + (g & 3)) * p.q_sh;
   uint32_t qb[KB][2];
-  float qf[KB][4];
 #pragma unroll
   for (int kb = 0; kb < KB; ++kb) {
     qb[kb][0] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t);
     qb[kb][1] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t + 8);
-    const float2 lo = O::unpack(qb[kb][0]), hi = O::unpack(qb[kb][1]);
-    qf[kb][0] = lo.x; qf[kb][1] = lo.y; qf[kb][2] = hi.x; qf[kb][3] = hi.y;
   }
+  // query rotated to the page start of this thread's column, advanced by
+  // R(-64) from one tile of the warp to its next (8 units = 64 positions on)
+  float rq[KB][4];
+  int rq_pos = -1;
+  float stc[KB / 2][4], sts[KB / 2][4];
+  const bool can_step = p.rope_rows > 64;
+#pragma unroll
+  for (int kb = 0; kb < KB / 2; ++kb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
+      stc[kb][e] = can_step ? p.cos[64 * (D / 2) + d] : 1.f;
+      sts[kb][e] = can_step ? p.sin[64 * (D / 2) + d] : 0.f;
+    }
 
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   float o[KB][4];
@@ -252,121 +268,127 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
   for (int mb = 0; mb < KB; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.f;
 
   const int my_tiles = n_tiles > warp ? (n_tiles - warp + kWarps - 1) / kWarps : 0;
-  // prologue: fill the ring
-#pragma unroll
-  for (int i = 0; i < C::kStages - 1; ++i) {
-    if (i < my_tiles) {
-      const int ua = u0 + 2 * (warp + kWarps * i);
-      unsigned char* st = ring + (size_t)i * C::kStageBytes;
-      issue_unit<T, D>(p, unit_info(p, ua, u1, tbl, j0), b, kh, st, lane);
-      issue_unit<T, D>(p, unit_info(p, ua + 1, u1, tbl, j0), b, kh, st + C::kHalfBytes, lane);
-    }
-    cp_commit();
-  }
 
-  const int hh0 = 2 * (t & 1);  // heads of this thread's score / output columns
-  const int my_unit = t >> 1;   // unit of this thread's valid score columns
-  for (int i = 0; i < my_tiles; ++i) {
-    {  // keep kStages-1 tiles in flight
-      const int ni = i + C::kStages - 1;
-      if (ni < my_tiles) {
-        const int ua = u0 + 2 * (warp + kWarps * ni);
-        unsigned char* st = ring + (size_t)(ni % C::kStages) * C::kStageBytes;
-        issue_unit<T, D>(p, unit_info(p, ua, u1, tbl, j0), b, kh, st, lane);
-        issue_unit<T, D>(p, unit_info(p, ua + 1, u1, tbl, j0), b, kh, st + C::kHalfBytes, lane);
-      }
-      cp_commit();
-    }
-    cp_wait<C::kStages - 1>();
-    __syncwarp();
-    const int ua = u0 + 2 * (warp + kWarps * i);
-    const Unit UA = unit_info(p, ua, u1, tbl, j0), UB = unit_info(p, ua + 1, u1, tbl, j0);
-    // operand class of each unit's MMAs: 0 = KV dtype (fp units), 1 = fp16
-    // (int4 pages, whose fp16 scale/zero make fp16 the exact dequant type);
-    // a missing unit follows the other one
-    const int clsA = (UA.kind == 2 || (UA.kind == 0 && UB.kind == 2)) ? 1 : 0;
-    const int clsB = (UB.kind == 2 || (UB.kind == 0 && UA.kind == 2)) ? 1 : 0;
-    unsigned char* st = ring + (size_t)(i % C::kStages) * C::kStageBytes;
-    const uint32_t st_s = smem_u32(st);
+  const int hh0 = 2 * (t & 1);
+  const int my_unit = t >> 1;
 
-    // ---- B fragments of the query for this thread's column (unit g>>2) ----
+  // One 16-token tile.  MODE 1: both units int4 pages; MODE 2: both units
+  // full fp rows; MODE 0: anything else (sinks, region boundaries, partial
+  // or missing units).  The common modes compile to straight-line code.
+  auto tile = [&](auto mode_c, auto slots_c, int i, int ua, int kA, int kB, int vA, int vB,
+                  const unsigned char* st) {
+    constexpr int MODE = decltype(mode_c)::value;
+    constexpr int SLOTS = decltype(slots_c)::value;
+    constexpr bool I4 = MODE == 1, FP = MODE == 2;
+    constexpr int HS = I4 ? C::kPageBytes : C::kHalfBytes;  // bytes between the two units of a slot
+    const int clsA = I4 ? 1 : (FP ? 0 : ((kA == 2 || (kA == 0 && kB == 2)) ? 1 : 0));
+    const int clsB = I4 ? 1 : (FP ? 0 : ((kB == 2 || (kB == 0 && kA == 2)) ? 1 : 0));
+    const bool uniform = I4 || FP || !kBF || clsA == clsB;
+    const bool use_h = kBF && clsA == 1;  // uniform tile in fp16 while T is bf16
+    const int my_col_kind = I4 ? 2 : (FP ? 1 : ((g >> 2) ? kB : kA));
+
+    // ---- query B fragments for this thread's column ----
     uint32_t qB[KB][2];
-    {
-      if (((g >> 2) ? UB.kind : UA.kind) == 2) {
-        const float* cs = reinterpret_cast<const float*>(st + (g >> 2) * C::kHalfBytes + C::kPageBytes);
-        const float* sn = cs + D / 2;
+    if (my_col_kind == 2) {
+      const int P = p.s + 8 * ((ua + (g >> 2)) - p.NS);
+      if (P != rq_pos) {  // seed from the table (first tier tile of this warp)
 #pragma unroll
-        for (int kb = 0; kb < KB / 2; ++kb) {
-          const float2 c0 = *reinterpret_cast<const float2*>(cs + 16 * kb + 2 * t);
-          const float2 c1 = *reinterpret_cast<const float2*>(cs + 16 * kb + 2 * t + 8);
-          const float2 s0 = *reinterpret_cast<const float2*>(sn + 16 * kb + 2 * t);
-          const float2 s1 = *reinterpret_cast<const float2*>(sn + 16 * kb + 2 * t + 8);
-          const float cc[4] = {c0.x, c0.y, c1.x, c1.y}, ss[4] = {s0.x, s0.y, s1.x, s1.y};
-          float xr[4], yr[4];
+        for (int kb = 0; kb < KB / 2; ++kb)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float x = qf[kb][e], y = qf[kb + KB / 2][e];
-            xr[e] = fmaf(x, cc[e], y * ss[e]);
-            yr[e] = fmaf(y, cc[e], -x * ss[e]);
+            const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
+            const float c = p.cos[(int64_t)P * (D / 2) + d], s = p.sin[(int64_t)P * (D / 2) + d];
+            const float x = ld_f32(qp + d), y = ld_f32(qp + d + D / 2);
+            rq[kb][e] = fmaf(x, c, y * s);
+            rq[kb + KB / 2][e] = fmaf(y, c, -x * s);
           }
-          qB[kb][0] = H::pack(xr[0], xr[1]);
-          qB[kb][1] = H::pack(xr[2], xr[3]);
-          qB[kb + KB / 2][0] = H::pack(yr[0], yr[1]);
-          qB[kb + KB / 2][1] = H::pack(yr[2], yr[3]);
-        }
-      } else {
-#pragma unroll
-        for (int kb = 0; kb < KB; ++kb) { qB[kb][0] = qb[kb][0]; qB[kb][1] = qb[kb][1]; }
       }
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) {
+        qB[kb][0] = H::pack(rq[kb][0], rq[kb][1]);
+        qB[kb][1] = H::pack(rq[kb][2], rq[kb][3]);
+      }
+      if (can_step) {  // advance to this warp's next tile: R(-(P+64)) q = R(-64) R(-P) q
+#pragma unroll
+        for (int kb = 0; kb < KB / 2; ++kb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float x = rq[kb][e], y = rq[kb + KB / 2][e];
+            rq[kb][e] = fmaf(x, stc[kb][e], y * sts[kb][e]);
+            rq[kb + KB / 2][e] = fmaf(y, stc[kb][e], -x * sts[kb][e]);
+          }
+        rq_pos = P + 64;
+      } else {
+        rq_pos = -1;
+      }
+    } else {
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) { qB[kb][0] = qb[kb][0]; qB[kb][1] = qb[kb][1]; }
     }
+
+    cp_wait<SLOTS - 1>();
+    __syncwarp();
+    const uint32_t st_s = smem_u32(st);
 
     // ---- S = K q (16 tokens x 8 columns) ----
     float sacc[4] = {0.f, 0.f, 0.f, 0.f};
     {
-      uint32_t ka[2][KB][2];  // [unit][kb][lo/hi 8 columns]
+      uint32_t ka[2][KB][2];  // [unit][kb][columns lo/hi]
+      auto k_int4 = [&](int h) {
+        const unsigned char* pg = st + h * HS;
+        uint32_t w[NW], sz[NW];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t hb = st_s + h * C::kHalfBytes;
-        if ((h ? UB.kind : UA.kind) == 2) {
-          const unsigned char* pg = st + h * C::kHalfBytes;
-          uint32_t w[NW];
-#pragma unroll
-          for (int e = 0; e < NW; ++e)
-            w[e] = reinterpret_cast<const uint32_t*>(pg)[(g * 4 + t) * NW + e];
-          uint32_t sz[NW];
-#pragma unroll
-          for (int e = 0; e < NW; ++e)
-            sz[e] = reinterpret_cast<const uint32_t*>(pg + page_k_scales_off(D))[g * NW + e];
-#pragma unroll
-          for (int kb = 0; kb < KB; ++kb) {
-            const uint32_t szw = sz[kb >> 1];
-            const uint32_t s2 = __byte_perm(szw, szw, 0x1010);
-            const uint32_t z2 = __byte_perm(szw, szw, 0x3232);
-            ka[h][kb][0] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1)), s2, z2);
-            ka[h][kb][1] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1) + 1), s2, z2);
-          }
-        } else {
-          const int r = lane & 7, sel = (lane >> 3) & 1;
-#pragma unroll
-          for (int kb = 0; kb < KB; ++kb)
-            ldsm_x2(ka[h][kb][0], ka[h][kb][1], hb + r * (2 * D) + (((2 * kb + sel) ^ r) * 16));
+        for (int e = 0; e < NW; ++e) {
+          w[e] = reinterpret_cast<const uint32_t*>(pg)[(g * 4 + t) * NW + e];
+          sz[e] = reinterpret_cast<const uint32_t*>(pg + page_k_scales_off(D))[g * NW + e];
         }
-      }
-      if (!kBF || clsA == clsB) {
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb) {
-          if (kBF && clsA == 1)
-            H::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
-          else
-            O::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+          const uint32_t szw = sz[kb >> 1];
+          const uint32_t s2 = __byte_perm(szw, szw, 0x1010), z2 = __byte_perm(szw, szw, 0x3232);
+          ka[h][kb][0] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1)), s2, z2);
+          ka[h][kb][1] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1) + 1), s2, z2);
         }
+      };
+      auto k_fp_half = [&](int h) {
+        const int r = lane & 7, sel = (lane >> 3) & 1;
+        const uint32_t hb = st_s + h * HS;
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          ldsm_x2(ka[h][kb][0], ka[h][kb][1], hb + r * (2 * D) + (((2 * kb + sel) ^ r) * 16));
+      };
+      if constexpr (FP) {
+        const int r = lane & 7, un = (lane >> 3) & 1, hi = lane >> 4;
+        const uint32_t rb = st_s + un * HS + r * (2 * D);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          ldsm_x4(ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], rb + (((2 * kb + hi) ^ r) * 16));
+      } else if constexpr (I4) {
+        k_int4(0);
+        k_int4(1);
+      } else {
+        if (kA == 2) k_int4(0); else k_fp_half(0);
+        if (kB == 2) k_int4(1); else k_fp_half(1);
+      }
+      if (uniform) {
+        float s2[4] = {0.f, 0.f, 0.f, 0.f};  // second chain: halves the MMA dependency depth
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb) {
+          float(&acc)[4] = (kb & 1) ? s2 : sacc;
+          if (I4 || use_h)
+            H::mma(acc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+          else
+            O::mma(acc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sacc[c] += s2[c];
       } else {
         // tier boundary in a bf16 cache: one MMA per operand type, the other
         // unit's rows and the other columns' query zeroed
         const bool colF16 = ((g >> 2) ? clsB : clsA) == 1;
+        const uint32_t n0 = clsA == 0 ? 0xFFFFFFFFu : 0u, n1 = clsB == 0 ? 0xFFFFFFFFu : 0u;
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb) {
-          const uint32_t n0 = clsA == 0 ? 0xFFFFFFFFu : 0u, n1 = clsB == 0 ? 0xFFFFFFFFu : 0u;
           O::mma(sacc, ka[0][kb][0] & n0, ka[1][kb][0] & n1, ka[0][kb][1] & n0, ka[1][kb][1] & n1,
                  colF16 ? 0u : qB[kb][0], colF16 ? 0u : qB[kb][1]);
           H::mma(sacc, ka[0][kb][0] & ~n0, ka[1][kb][0] & ~n1, ka[0][kb][1] & ~n0, ka[1][kb][1] & ~n1,
@@ -375,86 +397,85 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
       }
     }
 
-    // ---- online softmax (log2 domain) for this thread's two heads ----
-    const bool v = g < (my_unit ? UB.valid : UA.valid);
-    float sc[2];
-    sc[0] = v ? (my_unit ? sacc[2] : sacc[0]) * p.scale_log2 : -INFINITY;
-    sc[1] = v ? (my_unit ? sacc[3] : sacc[1]) * p.scale_log2 : -INFINITY;
-    float pr[2], alpha[2];
+    // ---- V^T fragments (independent of P: built while the QK MMAs run) ----
+    uint32_t va[2][KB][2];  // [unit][mb][d rows g / g+8]
+      auto v_int4 = [&](int h) {
+        const unsigned char* pg = st + h * HS;
+        uint32_t w[NW];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float mx = sc[e];
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float mn = fmaxf(m_run[e], mx);
-      alpha[e] = (mn == -INFINITY) ? 1.f : exp2f(m_run[e] - mn);
-      pr[e] = v ? exp2f(sc[e] - mn) : 0.f;
-      l_run[e] = l_run[e] * alpha[e] + pr[e];
-      m_run[e] = mn;
-    }
-#pragma unroll
-    for (int mb = 0; mb < KB; ++mb) {
-      o[mb][0] *= alpha[0]; o[mb][1] *= alpha[1];
-      o[mb][2] *= alpha[0]; o[mb][3] *= alpha[1];
-    }
-    // window mass of each unit: sum over its 8 rows
-    {
-      float ms0 = pr[0], ms1 = pr[1];
-      ms0 += __shfl_xor_sync(0xffffffffu, ms0, 4);
-      ms1 += __shfl_xor_sync(0xffffffffu, ms1, 4);
-      ms0 += __shfl_xor_sync(0xffffffffu, ms0, 8);
-      ms1 += __shfl_xor_sync(0xffffffffu, ms1, 8);
-      ms0 += __shfl_xor_sync(0xffffffffu, ms0, 16);
-      ms1 += __shfl_xor_sync(0xffffffffu, ms1, 16);
-      if (lane < 4) {
-        float* ms = mass_s + i * 12;
-        ms[my_unit * 4 + hh0] = ms0;
-        ms[my_unit * 4 + hh0 + 1] = ms1;
-        if (my_unit == 0) { ms[8 + hh0] = m_run[0]; ms[8 + hh0 + 1] = m_run[1]; }
-      }
-    }
-
-    // ---- O^T += V^T P ----
-    const float xa = my_unit == 0 ? pr[0] : 0.f, xb = my_unit == 0 ? pr[1] : 0.f;
-    const float ya = my_unit == 1 ? pr[0] : 0.f, yb = my_unit == 1 ? pr[1] : 0.f;
-    const uint32_t px = (kBF && clsA == 1) ? H::pack(xa, xb) : O::pack(xa, xb);
-    const uint32_t py = (kBF && clsB == 1) ? H::pack(ya, yb) : O::pack(ya, yb);
-    const uint32_t pb0 = movm_t(px), pb1 = movm_t(py);
-    {
-      uint32_t va[2][KB][2];  // [unit][mb][d rows g / g+8]
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t hb = st_s + h * C::kHalfBytes;
-        if ((h ? UB.kind : UA.kind) == 2) {
-          const unsigned char* pg = st + h * C::kHalfBytes;
-          uint32_t w[NW];
-#pragma unroll
-          for (int e = 0; e < NW; ++e)
-            w[e] = reinterpret_cast<const uint32_t*>(pg + page_v_codes_off(D))[(t * 8 + g) * NW + e];
-#pragma unroll
-          for (int mb = 0; mb < KB; ++mb) {
-            const uint2 sz = reinterpret_cast<const uint2*>(pg + page_v_scales_off(D))[t * NW + (mb >> 1)];
-            va[h][mb][0] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1)), sz.x, sz.y);
-            va[h][mb][1] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1) + 1), sz.x, sz.y);
-          }
-        } else {
-          const int r = lane & 7, sel = (lane >> 3) & 1;
-          const int nv = h ? UB.valid : UA.valid;
-          const uint32_t msk = (2 * t < nv ? 0x0000FFFFu : 0u) | (2 * t + 1 < nv ? 0xFFFF0000u : 0u);
-#pragma unroll
-          for (int mb = 0; mb < KB; ++mb) {
-            ldsm_x2_t(va[h][mb][0], va[h][mb][1], hb + 16 * D + r * (2 * D) + (((2 * mb + sel) ^ r) * 16));
-            va[h][mb][0] &= msk;
-            va[h][mb][1] &= msk;
-          }
-        }
-      }
-      if (!kBF || clsA == clsB) {
+        for (int e = 0; e < NW; ++e)
+          w[e] = reinterpret_cast<const uint32_t*>(pg + page_v_codes_off(D))[(t * 8 + g) * NW + e];
 #pragma unroll
         for (int mb = 0; mb < KB; ++mb) {
-          if (kBF && clsA == 1)
+          const uint2 sz = reinterpret_cast<const uint2*>(pg + page_v_scales_off(D))[t * NW + (mb >> 1)];
+          va[h][mb][0] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1)), sz.x, sz.y);
+          va[h][mb][1] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1) + 1), sz.x, sz.y);
+        }
+      };
+      auto v_fp_half = [&](int h, int nv) {
+        const int r = lane & 7, sel = (lane >> 3) & 1;
+        const uint32_t msk = (2 * t < nv ? 0x0000FFFFu : 0u) | (2 * t + 1 < nv ? 0xFFFF0000u : 0u);
+        const uint32_t hb = st_s + h * HS;
+#pragma unroll
+        for (int mb = 0; mb < KB; ++mb) {
+          ldsm_x2_t(va[h][mb][0], va[h][mb][1], hb + 16 * D + r * (2 * D) + (((2 * mb + sel) ^ r) * 16));
+          va[h][mb][0] &= msk;
+          va[h][mb][1] &= msk;
+        }
+      };
+      if constexpr (FP) {
+        const int r = lane & 7, sel = (lane >> 3) & 1, un = lane >> 4;
+        const uint32_t rb = st_s + un * HS + 16 * D + r * (2 * D);
+#pragma unroll
+        for (int mb = 0; mb < KB; ++mb)
+          ldsm_x4_t(va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], rb + (((2 * mb + sel) ^ r) * 16));
+      } else if constexpr (I4) {
+        v_int4(0);
+        v_int4(1);
+      } else {
+        if (kA == 2) v_int4(0); else v_fp_half(0, vA);
+        if (kB == 2) v_int4(1); else v_fp_half(1, vB);
+      }
+
+    // ---- softmax (log2 domain), rescaling only when a score passes the
+    //      running max by more than 2^kThresh ----
+    const bool v = (I4 || FP) ? true : (g < (my_unit ? vB : vA));
+    const float sc0 = v ? (my_unit ? sacc[2] : sacc[0]) * p.scale_log2 : -INFINITY;
+    const float sc1 = v ? (my_unit ? sacc[3] : sacc[1]) * p.scale_log2 : -INFINITY;
+    if (__any_sync(0xffffffffu, sc0 > m_run[0] + kThresh || sc1 > m_run[1] + kThresh)) {
+      float mx0 = sc0, mx1 = sc1;
+#pragma unroll
+      for (int off = 2; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+      const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m_run[0] - mn0);
+      const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m_run[1] - mn1);
+      l_run[0] *= al0;
+      l_run[1] *= al1;
+#pragma unroll
+      for (int mb = 0; mb < KB; ++mb) {
+        o[mb][0] *= al0; o[mb][1] *= al1;
+        o[mb][2] *= al0; o[mb][3] *= al1;
+      }
+      m_run[0] = mn0;
+      m_run[1] = mn1;
+    }
+    const float pr0 = v ? exp2f(sc0 - m_run[0]) : 0.f;
+    const float pr1 = v ? exp2f(sc1 - m_run[1]) : 0.f;
+    l_run[0] += pr0;
+    l_run[1] += pr1;
+    // ---- O^T += V^T P ----
+    const float xa = my_unit == 0 ? pr0 : 0.f, xb = my_unit == 0 ? pr1 : 0.f;
+    const float ya = my_unit == 1 ? pr0 : 0.f, yb = my_unit == 1 ? pr1 : 0.f;
+    const uint32_t pb0 = movm_t((I4 || (kBF && clsA == 1)) ? H::pack(xa, xb) : O::pack(xa, xb));
+    const uint32_t pb1 = movm_t((I4 || (kBF && clsB == 1)) ? H::pack(ya, yb) : O::pack(ya, yb));
+    {
+      if (uniform) {
+#pragma unroll
+        for (int mb = 0; mb < KB; ++mb) {
+          if (I4 || use_h)
             H::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
           else
             O::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
@@ -470,7 +491,84 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
         }
       }
     }
+    {  // window mass of each unit: sum over its 8 rows (exact fp32)
+      float ms0 = pr0, ms1 = pr1;
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        ms0 += __shfl_xor_sync(0xffffffffu, ms0, off);
+        ms1 += __shfl_xor_sync(0xffffffffu, ms1, off);
+      }
+      if (lane < 4) {
+        float* ms = mass_s + i * 12;
+        ms[my_unit * 4 + hh0] = ms0;
+        ms[my_unit * 4 + hh0 + 1] = ms1;
+        if (my_unit == 0) { ms[8 + hh0] = m_run[0]; ms[8 + hh0 + 1] = m_run[1]; }
+      }
+    }
+
     __syncwarp();
+  };
+
+  // A warp's tiles form a few homogeneous runs (sinks, int4 pages, fp rows,
+  // boundaries).  Each run streams through the ring with its own geometry:
+  // int4 tiles are small (two pages), so their runs keep many more tiles in
+  // flight; the ring drains between runs.
+  auto run_segment = [&](auto mode_c, auto slots_c, int i0, int i1) {
+    constexpr int MODE = decltype(mode_c)::value;
+    constexpr int SLOTS = decltype(slots_c)::value;
+    constexpr int HS = MODE == 1 ? C::kPageBytes : C::kHalfBytes;
+    constexpr int SLOT_BYTES = 2 * HS;
+    static_assert(SLOTS * SLOT_BYTES <= C::kStages * C::kStageBytes, "ring");
+#pragma unroll
+    for (int k = 0; k < SLOTS - 1; ++k) {
+      if (i0 + k < i1) {
+        const int ua = u0 + 2 * (warp + kWarps * (i0 + k));
+        unsigned char* sl = ring + k * SLOT_BYTES;
+        issue_unit(ua, sl);
+        issue_unit(ua + 1, sl + HS);
+      }
+      cp_commit();
+    }
+    int slot = 0, nslot = SLOTS - 1;
+    for (int i = i0; i < i1; ++i) {
+      if (i + SLOTS - 1 < i1) {
+        const int ua_n = u0 + 2 * (warp + kWarps * (i + SLOTS - 1));
+        unsigned char* sl = ring + nslot * SLOT_BYTES;
+        issue_unit(ua_n, sl);
+        issue_unit(ua_n + 1, sl + HS);
+      }
+      cp_commit();
+      nslot = nslot + 1 == SLOTS ? 0 : nslot + 1;
+      const int ua = u0 + 2 * (warp + kWarps * i);
+      const int kA = MODE == 1 ? 2 : (MODE == 2 ? 1 : R.kind(ua));
+      const int kB = MODE == 1 ? 2 : (MODE == 2 ? 1 : R.kind(ua + 1));
+      const int vA = MODE != 0 ? 8 : (kA == 2 ? 8 : (kA == 1 ? fp_valid(p, R, ua) : 0));
+      const int vB = MODE != 0 ? 8 : (kB == 2 ? 8 : (kB == 1 ? fp_valid(p, R, ua + 1) : 0));
+      tile(mode_c, slots_c, i, ua, kA, kB, vA, vB, ring + slot * SLOT_BYTES);
+      slot = slot + 1 == SLOTS ? 0 : slot + 1;
+    }
+  };
+  auto tile_mode = [&](int i) -> int {
+    const int ua = u0 + 2 * (warp + kWarps * i);
+    const int kA = R.kind(ua), kB = R.kind(ua + 1);
+    if (kA == 2 && kB == 2) return 1;
+    if (kA == 1 && kB == 1 && fp_valid(p, R, ua) == 8 && fp_valid(p, R, ua + 1) == 8) return 2;
+    return 0;
+  };
+  constexpr int kI4Slots = (int)(C::kStages * C::kStageBytes / (2 * C::kPageBytes)) < 8
+                               ? (int)(C::kStages * C::kStageBytes / (2 * C::kPageBytes))
+                               : 8;
+  for (int i = 0; i < my_tiles;) {
+    const int m = tile_mode(i);
+    int j = i + 1;
+    while (j < my_tiles && tile_mode(j) == m) ++j;
+    if (m == 1)
+      run_segment(std::integral_constant<int, 1>{}, std::integral_constant<int, kI4Slots>{}, i, j);
+    else if (m == 2)
+      run_segment(std::integral_constant<int, 2>{}, std::integral_constant<int, C::kStages>{}, i, j);
+    else
+      run_segment(std::integral_constant<int, 0>{}, std::integral_constant<int, C::kStages>{}, i, j);
+    i = j;
   }
   cp_wait<0>();
 
@@ -478,10 +576,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     float l = l_run[e];
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    l += __shfl_xor_sync(0xffffffffu, l, 4);
-    l += __shfl_xor_sync(0xffffffffu, l, 8);
-    l += __shfl_xor_sync(0xffffffffu, l, 16);
+#pragma unroll
+    for (int off = 2; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
     l_run[e] = l;
   }
 #pragma unroll
@@ -536,93 +632,100 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
   const float* msw = reinterpret_cast<const float*>(smem + C::kRingBytes) + warp * kMaxTilesPerWarp * 12;
   for (int e = lane; e < my_tiles * 8; e += 32) {
     const int i = e >> 3, h = (e >> 2) & 1, hh = e & 3;
-    const int ua = u0 + 2 * (warp + kWarps * i);
-    const int u = ua + h;
-    if (u >= u1) continue;
-    int window;
-    if (u < p.NS) window = -1;
-    else window = u - p.NS;  // tier page j -> window j; rest unit r -> n_tp + r
-    if (window < 0) continue;
+    const int u = u0 + 2 * (warp + kWarps * i) + h;
+    if (u >= u1 || u < p.NS) continue;
     const float mt = msw[i * 12 + 8 + hh];
     const float val = (mt == -INFINITY) ? 0.f : msw[i * 12 + h * 4 + hh] * exp2f(mt - s_M[hh]);
-    p.mass[((int64_t)b * p.Hkv * 4 + kh * 4 + hh) * p.W + window] = val;
+    p.mass[((int64_t)b * p.Hkv * 4 + kh * 4 + hh) * p.W + (u - p.NS)] = val;
   }
 }
 
+// Combine the splits of one (row, query head): blockIdx.x == 0 writes the
+// output, every block adds the normalised mass of its window chunk.
+constexpr int kMergeThreads = 128;
+constexpr int kMergeWindows = 4 * kMergeThreads;  // windows per block
+
 template <typename T, int D>
-__global__ void __launch_bounds__(128) decode_mma_merge_kernel(const __grid_constant__ MmaParams p) {
-  const int b = blockIdx.y, h = blockIdx.x;
+__global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const __grid_constant__ MmaParams p) {
+  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h >> 2, hh = h & 3;
   const int Hq = p.Hkv * 4;
   __shared__ float s_f[kMaxSplits];
-  __shared__ float s_M, s_invL;
+  __shared__ float s_invL;
   const float* part = p.part + ((int64_t)b * p.Hkv + kh) * p.n_split * 4 * (D + 2);
-  if (threadIdx.x == 0) {
-    float M = -INFINITY;
-    for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, part[(s * 4 + hh) * (D + 2) + D]);
-    float L = 0.f;
-    for (int s = 0; s < p.n_split; ++s) {
-      const float ms = part[(s * 4 + hh) * (D + 2) + D];
-      const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
-      s_f[s] = f;
-      L += f * part[(s * 4 + hh) * (D + 2) + D + 1];
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float ms[2], ls[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int s = lane + 32 * k;
+      ms[k] = s < p.n_split ? part[(s * 4 + hh) * (D + 2) + D] : -INFINITY;
+      ls[k] = s < p.n_split ? part[(s * 4 + hh) * (D + 2) + D + 1] : 0.f;
     }
-    s_M = M;
-    s_invL = 1.f / L;
+    const float M = warp_max(fmaxf(ms[0], ms[1]));
+    float L = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float f = ms[k] == -INFINITY ? 0.f : exp2f(ms[k] - M);
+      if (lane + 32 * k < p.n_split) s_f[lane + 32 * k] = f;
+      L += f * ls[k];
+    }
+    L = warp_sum(L);
+    if (lane == 0) s_invL = 1.f / L;
   }
   __syncthreads();
   const float invL = s_invL;
-  for (int c = threadIdx.x; c < D; c += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < p.n_split; ++s) acc += s_f[s] * part[(s * 4 + hh) * (D + 2) + c];
-    st_f32((T*)p.out + b * p.o_sb + h * p.o_sh + c, acc * invL);
+  if (chunk == 0) {
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+      float acc = 0.f;
+      for (int s = 0; s < p.n_split; ++s) acc += s_f[s] * part[(s * 4 + hh) * (D + 2) + c];
+      st_f32((T*)p.out + b * p.o_sb + h * p.o_sh + c, acc * invL);
+    }
   }
   if (p.scores == nullptr) return;
-  const float* ms = p.mass + ((int64_t)b * Hq + h) * p.W;
-  float* acc = p.scores + ((int64_t)b * Hq + h) * p.scores_cap;
-  for (int w = threadIdx.x; w < p.W; w += blockDim.x) {
-    const int u = p.NS + w;
-    int lo = 0, hi = p.n_split - 1;  // split s with bnd[s] <= u < bnd[s+1]
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (p.bnd[mid] <= u) lo = mid; else hi = mid - 1;
-    }
-    acc[w] += ms[w] * s_f[lo] * invL;
+  const float* __restrict__ ms = p.mass + ((int64_t)b * Hq + h) * p.W;
+  float* __restrict__ acc = p.scores + ((int64_t)b * Hq + h) * p.scores_cap;
+  const int w_end = min(p.W, (chunk + 1) * kMergeWindows);
+  float mv[4], av[4];
+  int ws[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {  // issue all loads first
+    ws[k] = chunk * kMergeWindows + threadIdx.x + k * kMergeThreads;
+    mv[k] = ws[k] < w_end ? ms[ws[k]] : 0.f;
+    av[k] = ws[k] < w_end ? acc[ws[k]] : 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (ws[k] >= w_end) continue;
+    const int u = p.NS + ws[k];
+    int sp = 0;
+#pragma unroll 1
+    for (int step = 32; step > 0; step >>= 1)  // last split with bnd <= u
+      if (sp + step < p.n_split && p.bnd[sp + step] <= u) sp += step;
+    acc[ws[k]] = av[k] + mv[k] * s_f[sp] * invL;
   }
 }
 
 template <int D>
 void plan_splits(MmaParams& p) {
-  using C = Cfg<D>;
-  const double c_fp = 32.0 * D, c_i4 = (double)(C::kPageBytes + 4 * D);
-  const double total = p.NS * c_fp + p.n_tp * c_i4 + (p.U - p.NS - p.n_tp) * c_fp;
+  // Every 16-token tile costs about the same time whether it holds fp or int4
+  // units (the kernel is bound by per-tile latency, not bytes), so ranges
+  // hold equal unit counts; the split count fills whole waves of resident CTAs.
   const int units = p.B * p.Hkv;
-  const int resident = D == 64 ? 4 : 2;
-  int n = ceil_div(2 * 148 * resident, units > 0 ? units : 1);
+  const int slots = 148 * (D == 64 ? 4 : 2);
+  int n = max(1, (2 * slots) / max(1, units));
   n = max(n, ceil_div(p.U, kMaxUnitsPerSplit));
   n = min(n, kMaxSplits);
-  n = min(n, max(1, (p.U + 15) / 16));
-  auto unit_at = [&](double x) -> int {  // first unit whose cumulative cost reaches x
-    const double a = p.NS * c_fp, bcost = a + p.n_tp * c_i4;
-    if (x <= a) return (int)(x / c_fp);
-    if (x <= bcost) return p.NS + (int)((x - a) / c_i4);
-    return p.NS + p.n_tp + (int)((x - bcost) / c_fp);
-  };
+  n = min(n, max(1, p.U / 16));
+  int per = ceil_div(p.U, n);
+  per = (per + 1) & ~1;
   p.bnd[0] = 0;
   int k = 1;
-  for (int s = 1; s < n; ++s) {
-    int u = unit_at(total * s / n) & ~1;
-    u = max(u, p.bnd[k - 1] + 2);
-    if (u >= p.U) break;
-    if (u - p.bnd[k - 1] > kMaxUnitsPerSplit) u = p.bnd[k - 1] + kMaxUnitsPerSplit;
-    p.bnd[k++] = u;
-  }
-  while (p.U - p.bnd[k - 1] > kMaxUnitsPerSplit && k < kMaxSplits) {
-    p.bnd[k] = p.bnd[k - 1] + kMaxUnitsPerSplit;
+  while (p.bnd[k - 1] < p.U && k <= kMaxSplits) {
+    p.bnd[k] = min(p.U, p.bnd[k - 1] + per);
     ++k;
   }
-  p.bnd[k] = p.U;
-  p.n_split = k;
+  p.n_split = k - 1;
 }
 
 template <typename T, int D>
@@ -633,7 +736,8 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
   dim3 grid(p.n_split, p.Hkv, p.B);
   decode_mma_kernel<T, D><<<grid, kThreads, C::kSmemBytes, stream>>>(p);
   SKV_CHECK_LAUNCH();
-  decode_mma_merge_kernel<T, D><<<dim3(p.Hkv * 4, p.B), 128, 0, stream>>>(p);
+  const int chunks = p.scores ? max(1, ceil_div(p.W, kMergeWindows)) : 1;
+  decode_mma_merge_kernel<T, D><<<dim3(chunks, p.Hkv * 4, p.B), kMergeThreads, 0, stream>>>(p);
   SKV_CHECK_LAUNCH();
   return SKV_OK;
 }
@@ -679,6 +783,7 @@ int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, in
   p.U = p.NS + p.n_tp + ceil_div(p.rest, kPageTokens);
   p.W = T > p.s ? (T - p.s + kPageTokens - 1) / kPageTokens : 0;
   p.scale_log2 = scaling * kLog2e;
+  p.rope_rows = L->rope_positions;
   if (p.U == 0) return SKV_ERR_INVALID_ARG;
   switch (L->head_dim) {
     case 64: plan_splits<64>(p); break;

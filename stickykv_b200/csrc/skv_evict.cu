@@ -101,14 +101,31 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
         if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
       }
       __syncthreads();
-      if (tid == 0) {
-        int krem = s_krem, cum = 0, d = 255;
-        for (; d >= 0; --d) {
-          if (cum + hist[d] >= krem) break;
-          cum += hist[d];
+      if (tid < 32) {  // one warp finds the digit holding the krem-th largest key
+        const int krem = s_krem;
+        int cnt[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { cnt[q] = hist[255 - (tid * 8 + q)]; tot += cnt[q]; }
+        int incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (tid >= o) incl += y;
         }
-        s_krem = krem - cum;
-        s_thr = (uint64_t)d;
+        const int excl = incl - tot;
+        const unsigned own = __ballot_sync(0xffffffffu, excl < krem && krem <= incl);
+        if (tid == __ffs(own) - 1) {
+          int c = excl;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (c + cnt[q] >= krem) {
+              s_thr = (uint64_t)(255 - (tid * 8 + q));
+              s_krem = krem - c;
+              break;
+            }
+            c += cnt[q];
+          }
+        }
       }
       __syncthreads();
       prefix |= s_thr << shift;
@@ -135,27 +152,19 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
     if (kept(w)) ret[pos++] = w;
   for (int i = tid; i < p.local_w; i += nt) ret[k + i] = E + i;
   __syncthreads();
-  // 4. retained list, score and id gather, zero the next windows
+  // 4. retained list (the score/id gather runs in evict_gather_kernel)
   for (int j = tid; j < p.R; j += nt) {
     p.retained[(int64_t)b * p.R + j] = ret[j];
     if (p.retained_out) p.retained_out[(int64_t)b * p.scores_cap + j] = ret[j];
-    p.ids_dst[(int64_t)b * p.scores_cap + j] = p.ids_src[(int64_t)b * p.scores_cap + ret[j]];
-  }
-  // windows that appear before the next eviction start from zero score and
-  // take ids from the running counter (cache.py:180-213)
-  const int ztail = min(p.scores_cap - p.R, kTailWindows);
-  for (int i = tid; i < ztail; i += nt)
-    p.ids_dst[(int64_t)b * p.scores_cap + p.R + i] = p.next_window_id + i;
-  for (int e = tid; e < p.Hq * (p.R + ztail); e += nt) {
-    const int h = e / (p.R + ztail), j = e % (p.R + ztail);
-    float* dst = p.scores_dst + ((int64_t)b * p.Hq + h) * p.scores_cap;
-    dst[j] = j < p.R ? p.scores_src[((int64_t)b * p.Hq + h) * p.scores_cap + ret[j]] : 0.f;
   }
   if (!p.tier) return;
   // 5. int4 tier page table: kept tier windows keep their pages, entrants get
   //    the lowest free pages in chronological order.
   const int n_tw_old = p.n_tier_old_tok / p.ws;
   for (int i = tid; i < p.page_cap; i += nt) used[i] = 0;
+  __syncthreads();
+  const int n_cand = E - n_tw_old;  // kept fp windows can only come from [n_tw_old, E)
+  for (int c = tid; c < n_cand; c += nt) p.entrant[(int64_t)b * p.W + c] = -1;
   __syncthreads();
   for (int j = tid; j < k; j += nt) {
     const int w = ret[j];
@@ -165,9 +174,8 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
         used[pg] = 1;
         p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + i] = pg;
       }
-      p.entrant[(int64_t)b * k + j] = -1;
     } else {
-      p.entrant[(int64_t)b * k + j] = w;
+      p.entrant[(int64_t)b * p.W + (w - n_tw_old)] = j;  // candidate -> new tier slot
     }
   }
   __syncthreads();
@@ -197,14 +205,37 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   }
 }
 
+// Score and original-id gather (cache.py:271-283), one CTA per (query head,
+// row); windows that appear before the next eviction start at zero score and
+// take ids from the running counter (cache.py:180-213).
+__global__ void __launch_bounds__(256) evict_gather_kernel(EvictParams p) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int* __restrict__ ret = p.retained + (int64_t)b * p.R;
+  const float* __restrict__ src = p.scores_src + ((int64_t)b * p.Hq + h) * p.scores_cap;
+  float* __restrict__ dst = p.scores_dst + ((int64_t)b * p.Hq + h) * p.scores_cap;
+  const int ztail = min(p.scores_cap - p.R, kTailWindows);
+#pragma unroll 4
+  for (int j = threadIdx.x; j < p.R + ztail; j += blockDim.x) dst[j] = j < p.R ? src[ret[j]] : 0.f;
+  if (h == 0) {
+    const int64_t* __restrict__ is = p.ids_src + (int64_t)b * p.scores_cap;
+    int64_t* __restrict__ id = p.ids_dst + (int64_t)b * p.scores_cap;
+#pragma unroll 4
+    for (int j = threadIdx.x; j < p.R + ztail; j += blockDim.x)
+      id[j] = j < p.R ? is[ret[j]] : p.next_window_id + (j - p.R);
+  }
+}
+
 // Copy fp tokens that stay fp into the destination store, keys re-rotated.
+// One thread per (token, 16-byte vector of the first half of the channels):
+// it handles the vector and its rotation partner in the second half.
 template <typename T>
-__global__ void evict_move_kernel(EvictParams p, int n_fp_tok) {
+__global__ void __launch_bounds__(256) evict_move_kernel(EvictParams p, int n_fp_tok) {
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
   const int b = blockIdx.z, h = blockIdx.y;
-  const int half = p.D / 2;
+  const int half = p.D / 2, nvec = half / VE;
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)n_fp_tok * half) return;
-  const int tau = (int)(idx / half), i = (int)(idx % half);
+  if (idx >= (int64_t)n_fp_tok * nvec) return;
+  const int tau = (int)(idx / nvec), c0 = (int)(idx % nvec) * VE;
   const int s_eff = min(p.s, p.T_old);
   int old_pos, new_pos;
   if (tau < s_eff) {
@@ -219,68 +250,86 @@ __global__ void evict_move_kernel(EvictParams p, int n_fp_tok) {
   }
   const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
   const Geometry gn{p.s, p.s_pad, p.ws, p.T_new, p.n_tier_new_tok};
-  const int src = go.fp_slot(old_pos), dst = gn.fp_slot(new_pos);
-  const int64_t rs = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + src) * p.D;
-  const int64_t rd = (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + dst) * p.D;
+  const int64_t rs = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + go.fp_slot(old_pos)) * p.D;
+  const int64_t rd = (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + gn.fp_slot(new_pos)) * p.D;
   const T* ks = (const T*)p.k_src + rs;
   const T* vs = (const T*)p.v_src + rs;
   T* kd = (T*)p.k_dst + rd;
   T* vd = (T*)p.v_dst + rd;
-  float x = ld_f32(ks + i), y = ld_f32(ks + i + half);
-  rope_strip_apply<T>(x, y, p.cos[(int64_t)old_pos * half + i], p.sin[(int64_t)old_pos * half + i],
-                      p.cos[(int64_t)new_pos * half + i], p.sin[(int64_t)new_pos * half + i]);
-  st_f32(kd + i, x);
-  st_f32(kd + i + half, y);
-  vd[i] = vs[i];
-  vd[i + half] = vs[i + half];
+  union Vec { uint4 u; T e[VE]; };
+  Vec kx, ky, ox, oy;
+  kx.u = *reinterpret_cast<const uint4*>(ks + c0);
+  ky.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
+  float co[VE], so[VE], cn[VE], sn[VE];
+#pragma unroll
+  for (int e = 0; e < VE; e += 4) {
+    *reinterpret_cast<float4*>(co + e) = *reinterpret_cast<const float4*>(p.cos + (int64_t)old_pos * half + c0 + e);
+    *reinterpret_cast<float4*>(so + e) = *reinterpret_cast<const float4*>(p.sin + (int64_t)old_pos * half + c0 + e);
+    *reinterpret_cast<float4*>(cn + e) = *reinterpret_cast<const float4*>(p.cos + (int64_t)new_pos * half + c0 + e);
+    *reinterpret_cast<float4*>(sn + e) = *reinterpret_cast<const float4*>(p.sin + (int64_t)new_pos * half + c0 + e);
+  }
+#pragma unroll
+  for (int e = 0; e < VE; ++e) {
+    float x = Elt<T>::to_f32(kx.e[e]), y = Elt<T>::to_f32(ky.e[e]);
+    rope_strip_apply<T>(x, y, co[e], so[e], cn[e], sn[e]);
+    ox.e[e] = Elt<T>::from_f32(x);
+    oy.e[e] = Elt<T>::from_f32(y);
+  }
+  *reinterpret_cast<uint4*>(kd + c0) = ox.u;
+  *reinterpret_cast<uint4*>(kd + c0 + half) = oy.u;
+  *reinterpret_cast<uint4*>(vd + c0) = *reinterpret_cast<const uint4*>(vs + c0);
+  *reinterpret_cast<uint4*>(vd + c0 + half) = *reinterpret_cast<const uint4*>(vs + c0 + half);
 }
 
 // Quantise one 8-token page (keys rotated to the page frame) and pack it.
 // `kin(r, c)` / `vin(r, c)` give token r channel c as fp32; `pos0` is the
 // logical position of row 0 (row r sits at pos0 + r; the page starts at a
-// multiple of 8 past the sinks).  One warp; smem scratch of 2*8*D codes.
-template <typename KF, typename VF>
-__device__ void quantize_page_warp(KF kin, VF vin, int D, int pos0, const float* cos, const float* sin,
-                                   uint8_t* page, uint8_t* sc) {
+// multiple of 8 past the sinks).  One warp.  The page is first staged in
+// shared memory as fp32 (keys already in the page frame) with independent
+// loads, then each lane quantises one (token, group) of K or V.
+// Scratch: 2*8*D floats + 2*8*D code bytes per warp.
+template <int D, typename KF, typename VF>
+__device__ void quantize_page_warp(KF kin, VF vin, int pos0, const float* cos, const float* sin,
+                                   uint8_t* page, unsigned char* scratch) {
   const int lane = threadIdx.x & 31;
   const int half = D / 2, ng = D / kQGroup;
-  uint8_t* kc = sc;
-  uint8_t* vc = sc + 8 * D;
+  float* kf = reinterpret_cast<float*>(scratch);
+  float* vf = kf + 8 * D;
+  uint8_t* kc = reinterpret_cast<uint8_t*>(vf + 8 * D);
+  uint8_t* vc = kc + 8 * D;
+#pragma unroll
+  for (int idx = lane; idx < 8 * half; idx += 32) {
+    const int r = idx / half, cp = idx % half;
+    float x = kin(r, cp), y = kin(r, cp + half);
+    const int64_t pos = pos0 + r;
+    to_page_frame(x, y, cos[pos * half + cp], sin[pos * half + cp], cos[(int64_t)r * half + cp],
+                  sin[(int64_t)r * half + cp]);
+    kf[r * D + cp] = x;
+    kf[r * D + cp + half] = y;
+  }
+#pragma unroll
+  for (int idx = lane; idx < 8 * D; idx += 32) vf[idx] = vin(idx / D, idx % D);
+  __syncwarp();
   __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
   __half* vscl = reinterpret_cast<__half*>(page + page_v_scales_off(D));
   for (int task = lane; task < 2 * 8 * ng; task += 32) {
     const int which = task / (8 * ng);  // 0 = K, 1 = V
     const int r = (task / ng) % 8, gq = task % ng;
-    float v[kQGroup];
+    const float* src = (which ? vf : kf) + r * D + gq * kQGroup;
     float mn = FLT_MAX, mx = -FLT_MAX;
+#pragma unroll 8
     for (int e = 0; e < kQGroup; ++e) {
-      const int c = gq * kQGroup + e;
-      float val;
-      if (which == 0) {
-        const int cp = c % half;
-        float x = kin(r, cp), y = kin(r, cp + half);
-        const int pos = pos0 + r;
-        to_page_frame(x, y, cos[(int64_t)pos * half + cp], sin[(int64_t)pos * half + cp],
-                      cos[(int64_t)r * half + cp], sin[(int64_t)r * half + cp]);
-        val = c < half ? x : y;
-      } else {
-        val = vin(r, c);
-      }
-      v[e] = val;
-      mn = fminf(mn, val);
-      mx = fmaxf(mx, val);
+      mn = fminf(mn, src[e]);
+      mx = fmaxf(mx, src[e]);
     }
     const __half s16 = __float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), 15.f));
     const __half z16 = __float2half_rn(mn);
-    const float s = __half2float(s16), z = __half2float(z16);
+    const float sc = __half2float(s16), z = __half2float(z16);
     uint8_t* codes = (which ? vc : kc) + r * D + gq * kQGroup;
+#pragma unroll 8
     for (int e = 0; e < kQGroup; ++e) {
       int q = 0;
-      if (s != 0.f) {
-        float t = rintf(__fdiv_rn(__fsub_rn(v[e], z), s));
-        t = fminf(fmaxf(t, 0.f), 15.f);
-        q = (int)t;
-      }
+      if (sc != 0.f) q = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(src[e], z), sc)), 0.f), 15.f);
       codes[e] = (uint8_t)q;
     }
     if (which == 0) {
@@ -297,6 +346,7 @@ __device__ void quantize_page_warp(KF kin, VF vin, int D, int pos0, const float*
   for (int idx = lane; idx < 8 * 4 * ng; idx += 32) {
     const int r = idx / (4 * ng), t = (idx / ng) % 4, w = idx % ng;
     uint32_t word = 0;
+#pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int ch = 2 * t + 8 * (4 * w + i);
       word |= (uint32_t)kc[r * D + ch] << (4 * i);
@@ -308,6 +358,7 @@ __device__ void quantize_page_warp(KF kin, VF vin, int D, int pos0, const float*
   for (int idx = lane; idx < 4 * 8 * ng; idx += 32) {
     const int t = idx / (8 * ng), g = (idx / ng) % 8, w = idx % ng;
     uint32_t word = 0;
+#pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int ch = g + 8 * (4 * w + i);
       word |= (uint32_t)vc[(2 * t) * D + ch] << (4 * i);
@@ -318,34 +369,38 @@ __device__ void quantize_page_warp(KF kin, VF vin, int D, int pos0, const float*
   __syncwarp();
 }
 
+// shared scratch per warp for quantize_page_warp
+__host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D * 4 + 2 * 8 * D; }
+
 constexpr int kDemoteWarps = 4;
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(32 * kDemoteWarps) evict_demote_kernel(EvictParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int b = blockIdx.z, h = blockIdx.y;
   const int warp = threadIdx.x >> 5;
-  const int task = blockIdx.x * kDemoteWarps + warp;  // (j, page i)
-  if (task >= p.kprime * p.ppw) return;
-  const int j = task / p.ppw, pi = task % p.ppw;
-  const int w = p.entrant[(int64_t)b * p.kprime + j];
-  if (w < 0) return;
+  const int n_tw_old = p.n_tier_old_tok / p.ws;
+  const int task = blockIdx.x * kDemoteWarps + warp;  // (candidate window, page i)
+  if (task >= (p.E - n_tw_old) * p.ppw) return;
+  const int cand = task / p.ppw, pi = task % p.ppw;
+  const int j = p.entrant[(int64_t)b * p.W + cand];
+  if (j < 0) return;  // candidate window dropped
+  const int w = n_tw_old + cand;
   const int pos0 = p.s + w * p.ws + pi * kPageTokens;
   const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
   const int slot0 = go.fp_slot(pos0);
   const int64_t rb = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + slot0) * p.D;
   const T* ks = (const T*)p.k_src + rb;
   const T* vs = (const T*)p.v_src + rb;
-  const int D = p.D;
   const int phys = p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + pi];
   uint8_t* page = p.pages + (((int64_t)b * p.Hkv + h) * p.page_cap + phys) * page_bytes(D);
-  quantize_page_warp([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
-                     [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, D, pos0, p.cos,
-                     p.sin, page, smem_raw + warp * 2 * 8 * D);
+  quantize_page_warp<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
+                        [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos,
+                        p.sin, page, smem_raw + warp * quant_scratch_bytes(D));
 }
 
-template <typename T>
-__global__ void __launch_bounds__(32 * kDemoteWarps) pack_pages_kernel(const T* k, const T* v, int D,
+template <typename T, int D>
+__global__ void __launch_bounds__(32 * kDemoteWarps) pack_pages_kernel(const T* k, const T* v,
                                                                        int first_pos, int n_pages,
                                                                        const float* cos, const float* sin,
                                                                        uint8_t* out) {
@@ -355,10 +410,10 @@ __global__ void __launch_bounds__(32 * kDemoteWarps) pack_pages_kernel(const T* 
   if (pg >= n_pages) return;
   const T* ks = k + (int64_t)pg * 8 * D;
   const T* vs = v + (int64_t)pg * 8 * D;
-  quantize_page_warp([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
-                     [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, D,
-                     first_pos + pg * 8, cos, sin, out + (int64_t)pg * page_bytes(D),
-                     smem_raw + warp * 2 * 8 * D);
+  quantize_page_warp<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
+                        [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); },
+                        first_pos + pg * 8, cos, sin, out + (int64_t)pg * page_bytes(D),
+                        smem_raw + warp * quant_scratch_bytes(D));
 }
 
 size_t select_smem_bytes(int E, int R, int page_cap) {
@@ -373,16 +428,25 @@ int launch_evict(EvictParams& p, cudaStream_t stream) {
   cudaFuncSetAttribute(evict_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   evict_select_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
   SKV_CHECK_LAUNCH();
+  evict_gather_kernel<<<dim3(p.Hq, p.B), 256, 0, stream>>>(p);
+  SKV_CHECK_LAUNCH();
   const int n_fp_tok = p.T_new - p.n_tier_new_tok;  // sinks + fp windows kept
   if (n_fp_tok > 0) {
-    const int64_t work = (int64_t)n_fp_tok * (p.D / 2);
+    const int64_t work = (int64_t)n_fp_tok * (p.D / 2) / (16 / (int)sizeof(T));
     dim3 grid((unsigned)ceil_div64(work, 256), p.Hkv, p.B);
     evict_move_kernel<T><<<grid, 256, 0, stream>>>(p, n_fp_tok);
     SKV_CHECK_LAUNCH();
   }
-  if (p.tier && p.kprime > 0) {
-    dim3 grid((unsigned)ceil_div(p.kprime * p.ppw, kDemoteWarps), p.Hkv, p.B);
-    evict_demote_kernel<T><<<grid, 32 * kDemoteWarps, kDemoteWarps * 2 * 8 * p.D, stream>>>(p);
+  const int n_cand = p.E - p.n_tier_old_tok / p.ws;
+  if (p.tier && p.kprime > 0 && n_cand > 0) {
+    dim3 grid((unsigned)ceil_div(n_cand * p.ppw, kDemoteWarps), p.Hkv, p.B);
+    const size_t sm = kDemoteWarps * quant_scratch_bytes(p.D);
+    switch (p.D) {
+      case 32: evict_demote_kernel<T, 32><<<grid, 32 * kDemoteWarps, sm, stream>>>(p); break;
+      case 64: evict_demote_kernel<T, 64><<<grid, 32 * kDemoteWarps, sm, stream>>>(p); break;
+      case 128: evict_demote_kernel<T, 128><<<grid, 32 * kDemoteWarps, sm, stream>>>(p); break;
+      default: return SKV_ERR_UNSUPPORTED;
+    }
     SKV_CHECK_LAUNCH();
   }
   return SKV_OK;
@@ -397,30 +461,29 @@ int evict_dispatch(EvictParams& p, cudaStream_t stream) {
   return SKV_ERR_UNSUPPORTED;
 }
 
-int pack_pages_dispatch(const skv_layer_desc* L, const void* k, const void* v, int first_pos,
-                        int n_pages, uint8_t* out, cudaStream_t stream) {
-  const int D = L->head_dim;
+template <typename T>
+int launch_pack(const void* k, const void* v, int D, int first_pos, int n_pages, const float* cos,
+                const float* sin, uint8_t* out, cudaStream_t stream) {
   dim3 grid(ceil_div(n_pages, kDemoteWarps));
-  const size_t smem = kDemoteWarps * 2 * 8 * D;
-  switch (L->kv_dtype) {
-    case SKV_F32:
-      pack_pages_kernel<float><<<grid, 32 * kDemoteWarps, smem, stream>>>(
-          (const float*)k, (const float*)v, D, first_pos, n_pages, L->rope_cos, L->rope_sin, out);
-      break;
-    case SKV_F16:
-      pack_pages_kernel<__half><<<grid, 32 * kDemoteWarps, smem, stream>>>(
-          (const __half*)k, (const __half*)v, D, first_pos, n_pages, L->rope_cos, L->rope_sin, out);
-      break;
-    case SKV_BF16:
-      pack_pages_kernel<__nv_bfloat16><<<grid, 32 * kDemoteWarps, smem, stream>>>(
-          (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, D, first_pos, n_pages, L->rope_cos,
-          L->rope_sin, out);
-      break;
-    default:
-      return SKV_ERR_UNSUPPORTED;
+  const size_t smem = kDemoteWarps * quant_scratch_bytes(D);
+  switch (D) {
+    case 32: pack_pages_kernel<T, 32><<<grid, 32 * kDemoteWarps, smem, stream>>>((const T*)k, (const T*)v, first_pos, n_pages, cos, sin, out); break;
+    case 64: pack_pages_kernel<T, 64><<<grid, 32 * kDemoteWarps, smem, stream>>>((const T*)k, (const T*)v, first_pos, n_pages, cos, sin, out); break;
+    case 128: pack_pages_kernel<T, 128><<<grid, 32 * kDemoteWarps, smem, stream>>>((const T*)k, (const T*)v, first_pos, n_pages, cos, sin, out); break;
+    default: return SKV_ERR_UNSUPPORTED;
   }
   SKV_CHECK_LAUNCH();
   return SKV_OK;
+}
+
+int pack_pages_dispatch(const skv_layer_desc* L, const void* k, const void* v, int first_pos,
+                        int n_pages, uint8_t* out, cudaStream_t stream) {
+  switch (L->kv_dtype) {
+    case SKV_F32: return launch_pack<float>(k, v, L->head_dim, first_pos, n_pages, L->rope_cos, L->rope_sin, out, stream);
+    case SKV_F16: return launch_pack<__half>(k, v, L->head_dim, first_pos, n_pages, L->rope_cos, L->rope_sin, out, stream);
+    case SKV_BF16: return launch_pack<__nv_bfloat16>(k, v, L->head_dim, first_pos, n_pages, L->rope_cos, L->rope_sin, out, stream);
+  }
+  return SKV_ERR_UNSUPPORTED;
 }
 
 }  // namespace skv
