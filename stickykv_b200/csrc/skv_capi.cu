@@ -20,6 +20,7 @@ int decode_generic(const skv_layer_desc* L, int T, int tier_pages, const void* q
                    int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float scaling, float* scores,
                    int scores_cap, void* ws, cudaStream_t stream);
 bool decode_mma_supported(const skv_layer_desc* L);
+bool decode_mma_length_ok(int T);
 size_t decode_mma_ws_size(const skv_layer_desc* L, int T);
 int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, int64_t q_sb,
                int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float scaling, float* scores,
@@ -180,7 +181,7 @@ int skv_decode_attention(const skv_layer_desc* L, int32_t T, int32_t tier_pages,
   if (!ws || ws_bytes < skv_decode_workspace_size(L, T)) return SKV_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return SKV_ERR_MISALIGNED;
   const cudaStream_t s = (cudaStream_t)stream;
-  if (decode_mma_supported(L) && T >= 16)
+  if (decode_mma_supported(L) && decode_mma_length_ok(T))
     return decode_mma(L, T, tier_pages, q, q_sb, q_sh, out, o_sb, o_sh, scaling, scores, scores_cap, ws, s);
   return decode_generic(L, T, tier_pages, q, q_sb, q_sh, out, o_sb, o_sh, scaling, scores, scores_cap, ws, s);
 }

@@ -8,22 +8,28 @@
 //
 // The retained cache of one (row, kv head) is a sequence of 8-token units:
 // [sink unit(s) | int4 tier pages | fp units after the tier].  With
-// window_size 8 every unit after the sinks is one scoring window.
+// window_size 8 every unit after the sinks is one scoring window.  A tile is
+// two consecutive units (16 tokens).
 //
 // Work split: one CTA per (row, kv head, unit range); ranges are balanced by
-// bytes (an fp unit moves 32*D bytes, an int4 page page_bytes + its cos/sin).
-// Each of the 4 warps streams its own 16-token tiles (two units) through a
-// private cp.async ring in shared memory, so the main loop has no CTA
-// barrier.  Per tile:
-//   QK  4 (or 8) mma.m16n8k16: rows = 16 tokens, columns = 4 heads x 2 units;
-//       unit A's keys only meet columns 0-3, unit B's columns 4-7, so each
-//       column group carries the query of its unit: unrotated for fp units,
-//       rotated to the page start R(-P) q for int4 pages (whose keys are
-//       stored in their page frame).  int4 codes are dequantised straight
-//       into the A fragment registers (one packed FMA per two channels).
-//   softmax in the log2 domain, online per warp; the window mass of each
-//       unit is the sum of its 8 rows, kept per warp with the running max.
-//   PV  4 (or 8) mma: O^T = V^T P, V^T fragments via ldmatrix.trans (fp) or
+// an estimated per-tile cost.  Each of the 4 warps takes a contiguous run of
+// the CTA's tiles (again cost-balanced) and streams it through a private
+// cp.async ring in shared memory, so the main loop has no CTA barrier.  A
+// warp's run splits into at most five homogeneous segments (sinks, int4
+// pages, tier/fp boundary, full fp units, ragged tail) whose bounds are
+// computed up front; int4 and full-fp segments run specialised straight-line
+// tile bodies with per-lane addresses fixed for the whole kernel.  Per tile:
+//   QK  mma.m16n8k16: rows = 16 tokens, columns = 4 heads x 2 units; unit A's
+//       keys only meet columns 0-3, unit B's columns 4-7, so each column
+//       group carries the query of its unit: unrotated for fp units, rotated
+//       to the page start R(-P) q (and pre-scaled into the log2 domain) for
+//       int4 pages, whose keys are stored in their page frame.  The rotated
+//       query steps R(-16) from one tile to the next (packed f32x2 math).
+//       int4 codes are expanded by magic-number OR into fp16 and dequantised
+//       with one packed FMA per two channels, straight into A fragments.
+//   softmax in the log2 domain, online per warp with lazy rescaling; the
+//       window mass of each unit is the sum of its 8 rows.
+//   PV  mma: O^T = V^T P, V^T fragments via ldmatrix.trans (fp) or
 //       dequantised codes (int4); P converted with movmatrix.trans.
 // The CTA merges its warps and writes (max, sum, O) and the window masses
 // relative to its max; a merge kernel combines the splits, writes the output
@@ -40,24 +46,30 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kMaxSplits = 64;
-constexpr int kMaxTilesPerWarp = 32;
-constexpr int kMaxUnitsPerSplit = 2 * kWarps * kMaxTilesPerWarp;
+constexpr int kMaxTilesPerCta = 128;
+constexpr int kMaxUnitsPerSplit = 2 * kMaxTilesPerCta;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kRotStep = 16;  // positions from one int4 tile of a warp to its next
 
 template <int D> struct Cfg {
-  static constexpr int kStages = 3;
-  static constexpr int kHalfBytes = 32 * D;           // one unit: fp K+V rows, or int4 page + cos/sin
+  static constexpr int kHalfBytes = 32 * D;           // one fp unit: 8 K rows + 8 V rows
+  static constexpr int kTileBytes = 2 * kHalfBytes;   // one fp tile slot
   static constexpr int kPageBytes = page_bytes(D);
   static constexpr int kCPR = D / 8;                  // 16-byte chunks per fp row
   static constexpr int kKB = D / 16;                  // k-blocks (QK) == m-blocks (PV)
   static constexpr int kNW = D / 32;                  // int4 words per (row, lane)
-  static constexpr size_t kStageBytes = 2 * kHalfBytes;
-  static constexpr size_t kRingBytes = (size_t)kWarps * kStages * kStageBytes;
-  static constexpr size_t kMassBytes = (size_t)kWarps * kMaxTilesPerWarp * 12 * 4;
+  static constexpr int kFpSlots = 3;
+  static constexpr int kWarpRing = kFpSlots * kTileBytes;
+  static constexpr int kI4Slots = kWarpRing / (2 * kPageBytes) < 8 ? kWarpRing / (2 * kPageBytes) : 8;
+  static constexpr size_t kRingBytes = (size_t)kWarps * kWarpRing;
+  static constexpr size_t kMassBytes = (size_t)kMaxTilesPerCta * 12 * 4;
   static constexpr size_t kTableBytes = (size_t)kMaxUnitsPerSplit * 4;
   static constexpr size_t kSmemBytes = kRingBytes + kMassBytes + kTableBytes;
-  static_assert(kPageBytes + 4 * D <= kHalfBytes, "int4 unit must fit a half stage");
+  static_assert(kI4Slots >= 2, "int4 ring");
 };
+
+// relative per-tile costs used to balance CTAs and warps
+constexpr int kCostGeneric = 5, kCostI4 = 3, kCostFp = 2;
 
 struct MmaParams {
   const void* k_fp;
@@ -84,12 +96,10 @@ struct MmaParams {
 __device__ __forceinline__ uint32_t u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ uint32_t u32(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
-__device__ __forceinline__ __nv_bfloat162 b2(uint32_t x) { return *reinterpret_cast<__nv_bfloat162*>(&x); }
 
 template <typename T> struct Op;
 template <> struct Op<__half> {
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return u32(__floats2half2_rn(lo, hi)); }
-  static __device__ __forceinline__ float2 unpack(uint32_t x) { return __half22float2(h2(x)); }
   static __device__ __forceinline__ void mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -98,20 +108,9 @@ template <> struct Op<__half> {
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
-  // nibbles i (low half) and i+4 (high half) of w as exact 16-bit values
-  static __device__ __forceinline__ uint32_t codes(uint32_t w, int i) {
-    const uint32_t x = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;   // 1024 + code
-    return u32(__hsub2(h2(x), h2(0x64006400u)));
-  }
-  // scale/zero stored as fp16 pairs -> operand pairs
-  static __device__ __forceinline__ uint32_t from_f16x2(uint32_t x) { return x; }
-  static __device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
-    return u32(__hfma2(h2(a), h2(b), h2(c)));
-  }
 };
 template <> struct Op<__nv_bfloat16> {
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return u32(__floats2bfloat162_rn(lo, hi)); }
-  static __device__ __forceinline__ float2 unpack(uint32_t x) { return __bfloat1622float2(b2(x)); }
   static __device__ __forceinline__ void mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -120,17 +119,26 @@ template <> struct Op<__nv_bfloat16> {
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
-  static __device__ __forceinline__ uint32_t codes(uint32_t w, int i) {
-    const uint32_t x = ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // 128 + code
-    return u32(__hsub2(b2(x), b2(0x43004300u)));
-  }
-  static __device__ __forceinline__ uint32_t from_f16x2(uint32_t x) {
-    return u32(__float22bfloat162_rn(__half22float2(h2(x))));
-  }
-  static __device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
-    return u32(__hfma2(b2(a), b2(b), b2(c)));
-  }
 };
+using H = Op<__half>;  // int4 pages are always computed in fp16 (their scale/zero are fp16)
+
+// int4 nibble pairs -> exact fp16 codes.  A word holds nibbles i (bits 4i..)
+// in its low half and i+4 in its high half.  Nibbles at bits 0-3 of a half
+// become 1024 + code when OR-ed into 0x6400 (1024.0, ulp 1); nibbles at bits
+// 4-7 become 64 + code when OR-ed into 0x5400 (64.0, ulp 1/16).  One shift
+// by 8 serves nibbles 2 and 3.  The subtraction is exact.
+template <int I>
+__device__ __forceinline__ uint32_t codes_f16(uint32_t lo, uint32_t hi) {
+  const uint32_t w = I < 2 ? lo : hi;
+  if constexpr ((I & 1) == 0) {
+    const uint32_t x = (w & 0x000F000Fu) | 0x64006400u;
+    return u32(__hsub2(h2(x), h2(0x64006400u)));
+  } else {
+    const uint32_t x = (w & 0x00F000F0u) | 0x54005400u;
+    return u32(__hsub2(h2(x), h2(0x54005400u)));
+  }
+}
+__device__ __forceinline__ uint32_t dq(uint32_t c, __half2 s, __half2 z) { return u32(__hfma2(h2(c), s, z)); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -164,6 +172,50 @@ __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
   return y;
 }
+template <int N> struct Words { uint32_t w[N]; };
+template <int N>
+__device__ __forceinline__ Words<N> lds_words(uint32_t addr) {
+  Words<N> r;
+  if constexpr (N == 2) {
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.w[0]), "=r"(r.w[1]) : "r"(addr));
+  } else {
+    static_assert(N % 4 == 0, "words");
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k)
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                   : "=r"(r.w[4 * k]), "=r"(r.w[4 * k + 1]), "=r"(r.w[4 * k + 2]), "=r"(r.w[4 * k + 3])
+                   : "r"(addr + 16 * k));
+  }
+  return r;
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+// (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1), one packed fp32 FMA
+__device__ __forceinline__ void fma_x2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                       float c1) {
+  asm("{.reg .b64 ra, rb, rc, rd;\n"
+      " mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n mov.b64 rc, {%6,%7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0,%1}, rd;}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void mul_x2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{.reg .b64 ra, rb, rd;\n"
+      " mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
+      " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// programmatic dependent launch (the merge kernel follows the decode kernel)
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
+
+// floor division by 2 for possibly negative numerators
+__device__ __forceinline__ int ceil_half(int x) { return (x + 1) >> 1; }
 
 // Unit kinds: 0 none, 1 fp (KV dtype rows in the fp store), 2 int4 page.
 struct Regions {
@@ -178,16 +230,37 @@ __device__ __forceinline__ int fp_valid(const MmaParams& p, const Regions& R, in
   return u < R.NS ? min(8, p.s_eff - 8 * u) : min(8, p.rest - 8 * (u - R.TB));
 }
 
+// Tile classes of one CTA, in tile order: generic [0,ia) | int4 [ia,ib) |
+// generic [ib,fa) | full fp [fa,fb) | generic [fb,n).
+struct TileRuns {
+  int ia, ib, fa, fb, n;
+  __device__ __forceinline__ int cost_before(int i) const {  // cost of tiles [0, i)
+    const int c_i4 = max(0, min(i, ib) - ia), c_fp = max(0, min(i, fb) - fa);
+    return kCostGeneric * (i - c_i4 - c_fp) + kCostI4 * c_i4 + kCostFp * c_fp;
+  }
+  // smallest i with cost_before(i) >= target
+  __device__ __forceinline__ int at_cost(int target) const {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (cost_before(mid) >= target) hi = mid; else lo = mid + 1;
+    }
+    return lo;
+  }
+};
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(const __grid_constant__ MmaParams p) {
   using C = Cfg<D>;
   using O = Op<T>;        // fp units: the KV dtype
-  using H = Op<__half>;   // int4 pages: fp16 (their scale/zero are fp16)
   constexpr bool kBF = !std::is_same<T, __half>::value;
-  constexpr int KB = C::kKB, NW = C::kNW;
-  constexpr int FP_IT = 8 * C::kCPR / 32;                 // cp.async per lane per fp tensor
-  constexpr int PG_CH = C::kPageBytes / 16;               // 16-byte chunks per page
+  constexpr int KB = C::kKB, NW = C::kNW, PB = C::kPageBytes, HS = C::kHalfBytes;
+  constexpr int FPJ = C::kCPR / 2;                        // cp.async per lane per fp tensor per tile
+  constexpr int FP_PER = C::kCPR / 4;                     // swizzle period of those chunks
+  constexpr int FP_IT = 8 * C::kCPR / 32;                 // cp.async per lane per fp tensor per unit
+  constexpr int PG_CH = PB / 16;                          // 16-byte chunks per page
   constexpr int PG_IT = (PG_CH + 31) / 32;
+  constexpr int I4_IT = (2 * PG_CH + 31) / 32;            // chunks per lane for a page pair
   constexpr float kThresh = 8.f;                          // lazy rescale margin (log2 domain)
   extern __shared__ __align__(128) unsigned char smem[];
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -196,192 +269,415 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   const int u0 = p.bnd[split], u1 = p.bnd[split + 1];
   const int n_tiles = (u1 - u0 + 1) >> 1;
   const Regions R{p.NS, p.NS + p.n_tp, p.U, u1};
+  grid_launch_dependents();  // the merge kernel waits for this grid's completion itself
 
-  unsigned char* ring = smem + (size_t)warp * C::kStages * C::kStageBytes;
-  float* mass_s = reinterpret_cast<float*>(smem + C::kRingBytes) + warp * kMaxTilesPerWarp * 12;
-  int* tbl = reinterpret_cast<int*>(smem + C::kRingBytes + C::kMassBytes);
+  unsigned char* ring = smem + (size_t)warp * C::kWarpRing;
+  const uint32_t ring_s = smem_u32(ring);
+  float* mass_s = reinterpret_cast<float*>(smem + C::kRingBytes);  // [tile][12]
+  int* tbl = reinterpret_cast<int*>(smem + C::kRingBytes + C::kMassBytes);  // [unit - u0]
 
-  const int j0 = max(0, u0 - p.NS), j1 = min(p.n_tp, max(0, u1 - p.NS));
-  for (int j = j0 + threadIdx.x; j < j1; j += kThreads) tbl[j - j0] = p.table[(int64_t)b * p.page_cap + j];
+  {  // page table slice, indexed by unit offset within the split
+    const int k0 = max(0, R.NS - u0), k1 = min(u1, R.TB) - u0;
+    const int32_t* src = p.table + (int64_t)b * p.page_cap + (u0 - R.NS);
+    for (int k = k0 + threadIdx.x; k < k1; k += kThreads) tbl[k] = src[k];
+  }
+
+  // tile classes and this warp's contiguous, cost-balanced run [tb, te)
+  TileRuns tr;
+  tr.n = n_tiles;
+  tr.ia = min(n_tiles, max(0, ceil_half(R.NS - u0)));
+  tr.ib = max(tr.ia, min(n_tiles, max(0, ceil_half(R.TB - 1 - u0))));
+  {
+    const int uf = min(R.TB + p.rest / 8, u1);  // first unit that is not a full fp unit
+    tr.fa = max(tr.ib, min(n_tiles, max(0, ceil_half(R.TB - u0))));
+    tr.fb = max(tr.fa, min(n_tiles, max(0, ceil_half(uf - 1 - u0))));
+  }
+  const int total = tr.cost_before(n_tiles);
+  const int tb = warp == 0 ? 0 : tr.at_cost((total * warp + kWarps - 1) / kWarps);
+  const int te = warp == kWarps - 1 ? n_tiles : tr.at_cost((total * (warp + 1) + kWarps - 1) / kWarps);
   __syncthreads();
 
-  // per-lane copy offsets (constant for the whole kernel)
-  uint32_t fp_soff[FP_IT];
-  int fp_goff[FP_IT];
-#pragma unroll
-  for (int j = 0; j < FP_IT; ++j) {
-    const int idx = lane + 32 * j, r = idx / C::kCPR, c = idx % C::kCPR;
-    fp_soff[j] = r * (2 * D) + ((c ^ (r & 7)) * 16);
-    fp_goff[j] = r * D + c * 8;
-  }
   const int64_t kv_row = ((int64_t)b * p.Hkv + kh) * p.cap * D;
   const int64_t pg_row = ((int64_t)b * p.Hkv + kh) * p.page_cap;
   const T* kfp = (const T*)p.k_fp + kv_row;
   const T* vfp = (const T*)p.v_fp + kv_row;
+  const unsigned char* pages_l = p.pages + pg_row * PB + lane * 16;
 
-  auto issue_unit = [&](int u, unsigned char* half) {
-    const int kd = R.kind(u);
-    const uint32_t hs = smem_u32(half);
-    if (kd == 1) {
-      const int64_t off = (int64_t)fp_slot0(p, R, u) * D;
-#pragma unroll
-      for (int j = 0; j < FP_IT; ++j) {
-        cp_async16(hs + fp_soff[j], kfp + off + fp_goff[j]);
-        cp_async16(hs + 16 * D + fp_soff[j], vfp + off + fp_goff[j]);
-      }
-    } else if (kd == 2) {
-      const uint8_t* pg = p.pages + (pg_row + tbl[u - p.NS - j0]) * C::kPageBytes;
-#pragma unroll
-      for (int j = 0; j < PG_IT; ++j) {
-        const int idx = lane + 32 * j;
-        if (idx < PG_CH) cp_async16(hs + idx * 16, pg + idx * 16);
-      }
-    }
-  };
+  // int4 page reads (per-lane offsets within a page)
+  const uint32_t kc_off = lane * NW * 4;  // (g*4 + t) words of NW
+  const uint32_t ks_off = page_k_scales_off(D) + g * NW * 4;
+  const uint32_t vc_off = page_v_codes_off(D) + (t * 8 + g) * NW * 4;
+  const uint32_t vs_off = page_v_scales_off(D) + t * NW * 8;
 
   // query of head (g & 3) in B-fragment order: d = 16kb + 2t + {0,1,8,9}
   const T* qp = (const T*)p.q + b * p.q_sb + (kh * 4 + (g & 3)) * p.q_sh;
-  uint32_t qb[KB][2];
-#pragma unroll
-  for (int kb = 0; kb < KB; ++kb) {
-    qb[kb][0] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t);
-    qb[kb][1] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t + 8);
-  }
-  // query rotated to the page start of this thread's column, advanced by
-  // R(-64) from one tile of the warp to its next (8 units = 64 positions on)
+  // query rotated to the page start of this thread's column (int4 columns)
   float rq[KB][4];
   int rq_pos = -1;
-  float stc[KB / 2][4], sts[KB / 2][4];
-  const bool can_step = p.rope_rows > 64;
+  const bool can_step = p.rope_rows > kRotStep;
+  // rq = scl * R(-P) q
+  auto seed = [&](int P, float scl) {
 #pragma unroll
-  for (int kb = 0; kb < KB / 2; ++kb)
+    for (int kb = 0; kb < KB / 2; ++kb)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
-      stc[kb][e] = can_step ? p.cos[64 * (D / 2) + d] : 1.f;
-      sts[kb][e] = can_step ? p.sin[64 * (D / 2) + d] : 0.f;
+      for (int e = 0; e < 4; ++e) {
+        const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
+        const float c = p.cos[(int64_t)P * (D / 2) + d], s = p.sin[(int64_t)P * (D / 2) + d];
+        const float x = ld_f32(qp + d), y = ld_f32(qp + d + D / 2);
+        rq[kb][e] = fmaf(x, c, y * s) * scl;
+        rq[kb + KB / 2][e] = fmaf(y, c, -x * s) * scl;
+      }
+  };
+  auto load_qb = [&](uint32_t (&qb)[KB][2]) {
+#pragma unroll
+    for (int kb = 0; kb < KB; ++kb) {
+      qb[kb][0] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t);
+      qb[kb][1] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t + 8);
     }
+  };
 
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float m_run[2] = {-INFINITY, -INFINITY}, m_thr[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   float o[KB][4];
 #pragma unroll
   for (int mb = 0; mb < KB; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.f;
 
-  const int my_tiles = n_tiles > warp ? (n_tiles - warp + kWarps - 1) / kWarps : 0;
-
   const int hh0 = 2 * (t & 1);
   const int my_unit = t >> 1;
+  const uint32_t maskA = my_unit ? 0u : 0xFFFFFFFFu;
 
-  // One 16-token tile.  MODE 1: both units int4 pages; MODE 2: both units
-  // full fp rows; MODE 0: anything else (sinks, region boundaries, partial
-  // or missing units).  The common modes compile to straight-line code.
-  auto tile = [&](auto mode_c, auto slots_c, int i, int ua, int kA, int kB, int vA, int vB,
-                  const unsigned char* st) {
-    constexpr int MODE = decltype(mode_c)::value;
-    constexpr int SLOTS = decltype(slots_c)::value;
-    constexpr bool I4 = MODE == 1, FP = MODE == 2;
-    constexpr int HS = I4 ? C::kPageBytes : C::kHalfBytes;  // bytes between the two units of a slot
-    const int clsA = I4 ? 1 : (FP ? 0 : ((kA == 2 || (kA == 0 && kB == 2)) ? 1 : 0));
-    const int clsB = I4 ? 1 : (FP ? 0 : ((kB == 2 || (kB == 0 && kA == 2)) ? 1 : 0));
-    const bool uniform = I4 || FP || !kBF || clsA == clsB;
-    const bool use_h = kBF && clsA == 1;  // uniform tile in fp16 while T is bf16
-    const int my_col_kind = I4 ? 2 : (FP ? 1 : ((g >> 2) ? kB : kA));
+  // int4 page -> K A-fragments (rows g of the page) and V^T A-fragments
+  auto page_k = [&](uint32_t pg, uint32_t (&ka)[KB][2]) {
+    const Words<NW> w = lds_words<NW>(pg + kc_off);
+    const Words<NW> sz = lds_words<NW>(pg + ks_off);
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+      const uint32_t lo = w.w[q], hi = w.w[q] >> 8;
+      const __half2 s2 = __low2half2(h2(sz.w[q])), z2 = __high2half2(h2(sz.w[q]));
+      ka[2 * q][0] = dq(codes_f16<0>(lo, hi), s2, z2);
+      ka[2 * q][1] = dq(codes_f16<1>(lo, hi), s2, z2);
+      ka[2 * q + 1][0] = dq(codes_f16<2>(lo, hi), s2, z2);
+      ka[2 * q + 1][1] = dq(codes_f16<3>(lo, hi), s2, z2);
+    }
+  };
+  auto page_v = [&](uint32_t pg, uint32_t (&va)[KB][2]) {
+    const Words<NW> w = lds_words<NW>(pg + vc_off);
+    const Words<2 * NW> sz = lds_words<2 * NW>(pg + vs_off);
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+      const uint32_t lo = w.w[q], hi = w.w[q] >> 8;
+      const __half2 s2 = h2(sz.w[2 * q]), z2 = h2(sz.w[2 * q + 1]);
+      va[2 * q][0] = dq(codes_f16<0>(lo, hi), s2, z2);
+      va[2 * q][1] = dq(codes_f16<1>(lo, hi), s2, z2);
+      va[2 * q + 1][0] = dq(codes_f16<2>(lo, hi), s2, z2);
+      va[2 * q + 1][1] = dq(codes_f16<3>(lo, hi), s2, z2);
+    }
+  };
 
-    // ---- query B fragments for this thread's column ----
-    uint32_t qB[KB][2];
-    if (my_col_kind == 2) {
-      const int P = p.s + 8 * ((ua + (g >> 2)) - p.NS);
-      if (P != rq_pos) {  // seed from the table (first tier tile of this warp)
+  // ---- softmax (log2 domain) with lazy rescale, PV, window mass ----
+  // sc0/sc1: this thread's two scores (row g of its unit, heads hh0, hh0+1),
+  // -inf where the row holds no token.  kFp16P: P packed as fp16 for both
+  // units (int4 tile, or bf16 cache tile whose units are all int4).
+  auto softmax_pv = [&](float sc0, float sc1, bool guard, uint32_t (&va)[2][KB][2], int mode_pv,
+                        int clsA, int clsB, int i) {
+    if (__any_sync(0xffffffffu, sc0 > m_thr[0] || sc1 > m_thr[1])) {
+      float mx0 = sc0, mx1 = sc1;
 #pragma unroll
-        for (int kb = 0; kb < KB / 2; ++kb)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
-            const float c = p.cos[(int64_t)P * (D / 2) + d], s = p.sin[(int64_t)P * (D / 2) + d];
-            const float x = ld_f32(qp + d), y = ld_f32(qp + d + D / 2);
-            rq[kb][e] = fmaf(x, c, y * s);
-            rq[kb + KB / 2][e] = fmaf(y, c, -x * s);
-          }
+      for (int off = 2; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
       }
+      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+      const float al0 = mn0 == -INFINITY ? 1.f : ex2(m_run[0] - mn0);
+      const float al1 = mn1 == -INFINITY ? 1.f : ex2(m_run[1] - mn1);
+      l_run[0] *= al0;
+      l_run[1] *= al1;
+#pragma unroll
+      for (int mb = 0; mb < KB; ++mb) {
+        o[mb][0] *= al0; o[mb][1] *= al1;
+        o[mb][2] *= al0; o[mb][3] *= al1;
+      }
+      m_run[0] = mn0;
+      m_run[1] = mn1;
+      m_thr[0] = mn0 + kThresh;
+      m_thr[1] = mn1 + kThresh;
+    }
+    float pr0 = ex2(sc0 - m_run[0]);
+    float pr1 = ex2(sc1 - m_run[1]);
+    if (guard) {  // rows without a token (and nothing seen yet)
+      pr0 = sc0 == -INFINITY ? 0.f : pr0;
+      pr1 = sc1 == -INFINITY ? 0.f : pr1;
+    }
+    l_run[0] += pr0;
+    l_run[1] += pr1;
+    // ---- O^T += V^T P ----
+    if (mode_pv == 1) {  // one operand type for both units
+      const uint32_t pk = H::pack(pr0, pr1);
+      const uint32_t pb0 = movm_t(pk & maskA), pb1 = movm_t(pk & ~maskA);
+#pragma unroll
+      for (int mb = 0; mb < KB; ++mb) H::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
+    } else if (mode_pv == 2) {
+      const uint32_t pk = O::pack(pr0, pr1);
+      const uint32_t pb0 = movm_t(pk & maskA), pb1 = movm_t(pk & ~maskA);
+#pragma unroll
+      for (int mb = 0; mb < KB; ++mb) O::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
+    } else {
+      // bf16 cache, one int4 unit and one fp unit: one MMA per operand type
+      const float xa = my_unit == 0 ? pr0 : 0.f, xb = my_unit == 0 ? pr1 : 0.f;
+      const float ya = my_unit == 1 ? pr0 : 0.f, yb = my_unit == 1 ? pr1 : 0.f;
+      const uint32_t pb0 = movm_t(clsA == 1 ? H::pack(xa, xb) : O::pack(xa, xb));
+      const uint32_t pb1 = movm_t(clsB == 1 ? H::pack(ya, yb) : O::pack(ya, yb));
+      const uint32_t n0 = clsA == 0 ? 0xFFFFFFFFu : 0u, n1 = clsB == 0 ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+      for (int mb = 0; mb < KB; ++mb) {
+        O::mma(o[mb], va[0][mb][0] & n0, va[0][mb][1] & n0, va[1][mb][0] & n1, va[1][mb][1] & n1,
+               pb0 & n0, pb1 & n1);
+        H::mma(o[mb], va[0][mb][0] & ~n0, va[0][mb][1] & ~n0, va[1][mb][0] & ~n1, va[1][mb][1] & ~n1,
+               pb0 & ~n0, pb1 & ~n1);
+      }
+    }
+    // ---- window mass: sum of the unit's 8 rows per head (exact fp32) ----
+    // lanes g, g^1 swap one head each, then reduce over the remaining g bits
+    float a = (g & 1) ? pr1 : pr0;
+    const float other = (g & 1) ? pr0 : pr1;
+    a += __shfl_xor_sync(0xffffffffu, other, 4);
+    a += __shfl_xor_sync(0xffffffffu, a, 8);
+    a += __shfl_xor_sync(0xffffffffu, a, 16);
+    if (lane < 8) {  // g in {0,1}: head hh0 + g of unit t>>1
+      float* ms = mass_s + i * 12;
+      ms[my_unit * 4 + hh0 + g] = a;
+      if (lane < 2) *reinterpret_cast<float2*>(ms + 8 + hh0) = make_float2(m_run[0], m_run[1]);
+    }
+  };
+
+  // ======================= int4 tiles (both units pages) =======================
+  auto run_int4 = [&](int i0, int i1) {
+    constexpr int SL = C::kI4Slots, SB = 2 * PB;
+    auto issue = [&](int i, uint32_t dst) {
+      const int2 pr = *reinterpret_cast<const int2*>(tbl + 2 * i);
+      const unsigned char* pa = pages_l + (int64_t)pr.x * PB;
+      const unsigned char* pb = pages_l + (int64_t)pr.y * PB;
+#pragma unroll
+      for (int k = 0; k < I4_IT; ++k) {
+        const int c0 = 32 * k;  // chunk of lane 0
+        if (c0 + 31 < PG_CH) {
+          cp_async16(dst + 512 * k, pa + 512 * k);
+        } else if (c0 >= PG_CH) {
+          if (c0 + 31 < 2 * PG_CH || lane + c0 < 2 * PG_CH) cp_async16(dst + 512 * k, pb + (c0 - PG_CH) * 16);
+        } else {
+          const unsigned char* src = lane + c0 < PG_CH ? pa + 512 * k : pb + (c0 - PG_CH) * 16;
+          if (c0 + 31 < 2 * PG_CH || lane + c0 < 2 * PG_CH) cp_async16(dst + 512 * k, src);
+        }
+      }
+    };
+    const uint32_t dst_l = ring_s + lane * 16;
+#pragma unroll
+    for (int k = 0; k < SL - 1; ++k) {
+      if (i0 + k < i1) issue(i0 + k, dst_l + k * SB);
+      cp_commit();
+    }
+    // R(-16) step for this thread's channels; (c, s, -s)
+    float stc[KB / 2][4], sts[KB / 2][4], nst[KB / 2][4];
+#pragma unroll
+    for (int kb = 0; kb < KB / 2; ++kb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
+        stc[kb][e] = can_step ? p.cos[kRotStep * (D / 2) + d] : 1.f;
+        sts[kb][e] = can_step ? p.sin[kRotStep * (D / 2) + d] : 0.f;
+        nst[kb][e] = -sts[kb][e];
+      }
+    // query of this thread's column at the first tile
+    {
+      const int P = p.s + 8 * (u0 + 2 * i0 - R.NS + (g >> 2));
+      if (P != rq_pos) seed(P, p.scale_log2);
+    }
+    uint32_t cs = ring_s, is = ring_s + (SL - 1) * SB;
+    for (int i = i0; i < i1; ++i) {
+      if (!can_step && i > i0) seed(p.s + 8 * (u0 + 2 * i - R.NS + (g >> 2)), p.scale_log2);
+      if (i + SL - 1 < i1) issue(i + SL - 1, is + lane * 16);
+      cp_commit();
+      is = is + SB == ring_s + SL * SB ? ring_s : is + SB;
+      uint32_t qB[KB][2];
 #pragma unroll
       for (int kb = 0; kb < KB; ++kb) {
         qB[kb][0] = H::pack(rq[kb][0], rq[kb][1]);
         qB[kb][1] = H::pack(rq[kb][2], rq[kb][3]);
       }
-      if (can_step) {  // advance to this warp's next tile: R(-(P+64)) q = R(-64) R(-P) q
+      // advance the rotated query to this warp's next tile: R(-(P+16)) q
 #pragma unroll
-        for (int kb = 0; kb < KB / 2; ++kb)
+      for (int kb = 0; kb < KB / 2; ++kb)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float x = rq[kb][e], y = rq[kb + KB / 2][e];
-            rq[kb][e] = fmaf(x, stc[kb][e], y * sts[kb][e]);
-            rq[kb + KB / 2][e] = fmaf(y, stc[kb][e], -x * sts[kb][e]);
-          }
-        rq_pos = P + 64;
-      } else {
-        rq_pos = -1;
-      }
-    } else {
-#pragma unroll
-      for (int kb = 0; kb < KB; ++kb) { qB[kb][0] = qb[kb][0]; qB[kb][1] = qb[kb][1]; }
-    }
-
-    cp_wait<SLOTS - 1>();
-    __syncwarp();
-    const uint32_t st_s = smem_u32(st);
-
-    // ---- S = K q (16 tokens x 8 columns) ----
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      uint32_t ka[2][KB][2];  // [unit][kb][columns lo/hi]
-      auto k_int4 = [&](int h) {
-        const unsigned char* pg = st + h * HS;
-        uint32_t w[NW], sz[NW];
-#pragma unroll
-        for (int e = 0; e < NW; ++e) {
-          w[e] = reinterpret_cast<const uint32_t*>(pg)[(g * 4 + t) * NW + e];
-          sz[e] = reinterpret_cast<const uint32_t*>(pg + page_k_scales_off(D))[g * NW + e];
+        for (int e = 0; e < 4; e += 2) {
+          float ys0, ys1, xs0, xs1;
+          mul_x2(ys0, ys1, rq[kb + KB / 2][e], rq[kb + KB / 2][e + 1], sts[kb][e], sts[kb][e + 1]);
+          mul_x2(xs0, xs1, rq[kb][e], rq[kb][e + 1], nst[kb][e], nst[kb][e + 1]);
+          fma_x2(rq[kb][e], rq[kb][e + 1], rq[kb][e], rq[kb][e + 1], stc[kb][e], stc[kb][e + 1], ys0, ys1);
+          fma_x2(rq[kb + KB / 2][e], rq[kb + KB / 2][e + 1], rq[kb + KB / 2][e], rq[kb + KB / 2][e + 1],
+                 stc[kb][e], stc[kb][e + 1], xs0, xs1);
         }
+      cp_wait<SL - 1>();
+      __syncwarp();
+      uint32_t ka[2][KB][2], va[2][KB][2];
+      page_k(cs, ka[0]);
+      page_k(cs + PB, ka[1]);
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+        H::mma((kb & 1) ? s2 : sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+      page_v(cs, va[0]);
+      page_v(cs + PB, va[1]);
+      __syncwarp();
+      cs = cs + SB == ring_s + SL * SB ? ring_s : cs + SB;
+      const float sc0 = my_unit ? sacc[2] + s2[2] : sacc[0] + s2[0];
+      const float sc1 = my_unit ? sacc[3] + s2[3] : sacc[1] + s2[1];
+      softmax_pv(sc0, sc1, false, va, 1, 1, 1, i);
+    }
+    rq_pos = can_step ? p.s + 8 * (u0 + 2 * i1 - R.NS + (g >> 2)) : -1;
+  };
+
+  // ======================= full fp tiles =======================
+  auto run_fp = [&](int i0, int i1) {
+    constexpr int SL = C::kFpSlots, SB = C::kTileBytes;
+    uint32_t qb[KB][2];
+    load_qb(qb);
+    // chunk lane + 32j of a tile's 16 rows: rows advance 32/CPR per j, the
+    // swizzle repeats every FP_PER chunks, the unit every 8 rows
+    uint32_t fp_soff[FP_PER];
+#pragma unroll
+    for (int q = 0; q < FP_PER; ++q) {
+      const int r = lane / C::kCPR + q * (32 / C::kCPR), c = lane % C::kCPR;
+      fp_soff[q] = r * (2 * D) + ((c ^ r) * 16);
+    }
+    // ldmatrix: x4 matrices (unit, 8-channel chunk); offset of k-block kb is
+    // base ^ (kb << 5) because the swizzle XORs the chunk index with the row
+    const int lr = lane & 7;
+    const uint32_t k_base = ((lane >> 3) & 1) * HS + lr * (2 * D) + ((((lane >> 4) ^ lr) & 1) * 16) + ((lr >> 1) << 5);
+    const uint32_t v_base = (lane >> 4) * HS + 16 * D + lr * (2 * D) + (((((lane >> 3) & 1) ^ lr) & 1) * 16) + ((lr >> 1) << 5);
+    // global source of chunk lane + 32j: rows of unit pair, 512 bytes per j
+    const int64_t row0 = (int64_t)(p.s_pad + 8 * (u0 - R.TB)) * D;  // element offset of tile 0
+    const unsigned char* kg = reinterpret_cast<const unsigned char*>(kfp + row0) + lane * 16;
+    const unsigned char* vg = reinterpret_cast<const unsigned char*>(vfp + row0) + lane * 16;
+    auto issue = [&](int i, uint32_t slot) {
+      const int64_t off = (int64_t)i * 32 * D;  // 16 rows of D elements, in bytes
+#pragma unroll
+      for (int j = 0; j < FPJ; ++j) {
+        const uint32_t d = slot + fp_soff[j % FP_PER] + (j / FP_PER) * HS;
+        cp_async16(d, kg + off + 512 * j);
+        cp_async16(d + 16 * D, vg + off + 512 * j);
+      }
+    };
+#pragma unroll
+    for (int k = 0; k < SL - 1; ++k) {
+      if (i0 + k < i1) issue(i0 + k, ring_s + k * SB);
+      cp_commit();
+    }
+    uint32_t cs = ring_s, is = ring_s + (SL - 1) * SB;
+    for (int i = i0; i < i1; ++i) {
+      if (i + SL - 1 < i1) issue(i + SL - 1, is);
+      cp_commit();
+      is = is + SB == ring_s + SL * SB ? ring_s : is + SB;
+      cp_wait<SL - 1>();
+      __syncwarp();
+      uint32_t ka[2][KB][2], va[2][KB][2];
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+        ldsm_x4(ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], cs + (k_base ^ (kb << 5)));
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+        O::mma((kb & 1) ? s2 : sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qb[kb][0], qb[kb][1]);
+#pragma unroll
+      for (int mb = 0; mb < KB; ++mb)
+        ldsm_x4_t(va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], cs + (v_base ^ (mb << 5)));
+      __syncwarp();
+      cs = cs + SB == ring_s + SL * SB ? ring_s : cs + SB;
+      const float sc0 = (my_unit ? sacc[2] + s2[2] : sacc[0] + s2[0]) * p.scale_log2;
+      const float sc1 = (my_unit ? sacc[3] + s2[3] : sacc[1] + s2[1]) * p.scale_log2;
+      softmax_pv(sc0, sc1, false, va, 2, 0, 0, i);
+    }
+  };
+
+  // ======================= anything else (one tile at a time) =======================
+  // sinks, region boundaries, partial or missing units
+  auto issue_unit = [&](int u, uint32_t hs) {
+    const int kd = R.kind(u);
+    if (kd == 1) {
+      const int64_t off = (int64_t)fp_slot0(p, R, u) * D;
+#pragma unroll
+      for (int j = 0; j < FP_IT; ++j) {  // chunk lane + 32j of the unit's 8 rows
+        const int idx = lane + 32 * j, r = idx / C::kCPR, c = idx % C::kCPR;
+        const uint32_t so = r * (2 * D) + ((c ^ (r & 7)) * 16);
+        cp_async16(hs + so, kfp + off + r * D + c * 8);
+        cp_async16(hs + 16 * D + so, vfp + off + r * D + c * 8);
+      }
+    } else if (kd == 2) {
+      const unsigned char* pg = pages_l + (int64_t)tbl[u - u0] * PB;
+#pragma unroll
+      for (int j = 0; j < PG_IT; ++j)
+        if (lane + 32 * j < PG_CH) cp_async16(hs + lane * 16 + 512 * j, pg + 512 * j);
+    }
+  };
+  auto run_generic = [&](int i0, int i1) {
+    uint32_t qb[KB][2];
+    load_qb(qb);
+    for (int i = i0; i < i1; ++i) {
+      const int ua = u0 + 2 * i;
+      issue_unit(ua, ring_s);
+      issue_unit(ua + 1, ring_s + HS);
+      cp_commit();
+      const int kA = R.kind(ua), kB = R.kind(ua + 1);
+      const int vA = kA == 2 ? 8 : (kA == 1 ? fp_valid(p, R, ua) : 0);
+      const int vB = kB == 2 ? 8 : (kB == 1 ? fp_valid(p, R, ua + 1) : 0);
+      // operand class per unit: 1 = fp16 (int4 page, or missing unit next to one)
+      const int clsA = (kA == 2 || (kA == 0 && kB == 2)) ? 1 : 0;
+      const int clsB = (kB == 2 || (kB == 0 && kA == 2)) ? 1 : 0;
+      const bool uniform = !kBF || clsA == clsB;
+      const bool use_h = kBF && clsA == 1;
+      const int my_kind = (g >> 2) ? kB : kA;
+      uint32_t qB[KB][2];
+      if (my_kind == 2) {
+        seed(p.s + 8 * ((ua + (g >> 2)) - R.NS), 1.f);
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb) {
-          const uint32_t szw = sz[kb >> 1];
-          const uint32_t s2 = __byte_perm(szw, szw, 0x1010), z2 = __byte_perm(szw, szw, 0x3232);
-          ka[h][kb][0] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1)), s2, z2);
-          ka[h][kb][1] = H::fma2(H::codes(w[kb >> 1], 2 * (kb & 1) + 1), s2, z2);
+          qB[kb][0] = H::pack(rq[kb][0], rq[kb][1]);
+          qB[kb][1] = H::pack(rq[kb][2], rq[kb][3]);
         }
-      };
+      } else {
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb) { qB[kb][0] = qb[kb][0]; qB[kb][1] = qb[kb][1]; }
+      }
+      cp_wait<0>();
+      __syncwarp();
+      uint32_t ka[2][KB][2], va[2][KB][2];
       auto k_fp_half = [&](int h) {
         const int r = lane & 7, sel = (lane >> 3) & 1;
-        const uint32_t hb = st_s + h * HS;
+        const uint32_t hb = ring_s + h * HS;
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb)
           ldsm_x2(ka[h][kb][0], ka[h][kb][1], hb + r * (2 * D) + (((2 * kb + sel) ^ r) * 16));
       };
-      if constexpr (FP) {
-        const int r = lane & 7, un = (lane >> 3) & 1, hi = lane >> 4;
-        const uint32_t rb = st_s + un * HS + r * (2 * D);
+      auto v_fp_half = [&](int h, int nv) {
+        const int r = lane & 7, sel = (lane >> 3) & 1;
+        const uint32_t msk = (2 * t < nv ? 0x0000FFFFu : 0u) | (2 * t + 1 < nv ? 0xFFFF0000u : 0u);
+        const uint32_t hb = ring_s + h * HS;
 #pragma unroll
-        for (int kb = 0; kb < KB; ++kb)
-          ldsm_x4(ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], rb + (((2 * kb + hi) ^ r) * 16));
-      } else if constexpr (I4) {
-        k_int4(0);
-        k_int4(1);
-      } else {
-        if (kA == 2) k_int4(0); else k_fp_half(0);
-        if (kB == 2) k_int4(1); else k_fp_half(1);
-      }
+        for (int mb = 0; mb < KB; ++mb) {
+          ldsm_x2_t(va[h][mb][0], va[h][mb][1], hb + 16 * D + r * (2 * D) + (((2 * mb + sel) ^ r) * 16));
+          va[h][mb][0] &= msk;
+          va[h][mb][1] &= msk;
+        }
+      };
+      if (kA == 2) { page_k(ring_s, ka[0]); page_v(ring_s, va[0]); } else { k_fp_half(0); v_fp_half(0, vA); }
+      if (kB == 2) { page_k(ring_s + HS, ka[1]); page_v(ring_s + HS, va[1]); } else { k_fp_half(1); v_fp_half(1, vB); }
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
       if (uniform) {
-        float s2[4] = {0.f, 0.f, 0.f, 0.f};  // second chain: halves the MMA dependency depth
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb) {
-          float(&acc)[4] = (kb & 1) ? s2 : sacc;
-          if (I4 || use_h)
-            H::mma(acc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+          if (use_h || !kBF && clsA == 1)
+            H::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
           else
-            O::mma(acc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+            O::mma(sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) sacc[c] += s2[c];
       } else {
         // tier boundary in a bf16 cache: one MMA per operand type, the other
         // unit's rows and the other columns' query zeroed
@@ -395,180 +691,27 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
                  colF16 ? qB[kb][0] : 0u, colF16 ? qB[kb][1] : 0u);
         }
       }
+      __syncwarp();
+      const bool v = g < (my_unit ? vB : vA);
+      const float sc0 = v ? (my_unit ? sacc[2] : sacc[0]) * p.scale_log2 : -INFINITY;
+      const float sc1 = v ? (my_unit ? sacc[3] : sacc[1]) * p.scale_log2 : -INFINITY;
+      // P operand type: fp16 when the unit is an int4 page (any cache dtype)
+      // or the cache is fp16; else bf16.  Uniform tiles use one MMA type.
+      const int mode_pv = !uniform ? 0 : ((!kBF || clsA == 1) ? 1 : 2);
+      softmax_pv(sc0, sc1, true, va, mode_pv, clsA, clsB, i);
     }
-
-    // ---- V^T fragments (independent of P: built while the QK MMAs run) ----
-    uint32_t va[2][KB][2];  // [unit][mb][d rows g / g+8]
-      auto v_int4 = [&](int h) {
-        const unsigned char* pg = st + h * HS;
-        uint32_t w[NW];
-#pragma unroll
-        for (int e = 0; e < NW; ++e)
-          w[e] = reinterpret_cast<const uint32_t*>(pg + page_v_codes_off(D))[(t * 8 + g) * NW + e];
-#pragma unroll
-        for (int mb = 0; mb < KB; ++mb) {
-          const uint2 sz = reinterpret_cast<const uint2*>(pg + page_v_scales_off(D))[t * NW + (mb >> 1)];
-          va[h][mb][0] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1)), sz.x, sz.y);
-          va[h][mb][1] = H::fma2(H::codes(w[mb >> 1], 2 * (mb & 1) + 1), sz.x, sz.y);
-        }
-      };
-      auto v_fp_half = [&](int h, int nv) {
-        const int r = lane & 7, sel = (lane >> 3) & 1;
-        const uint32_t msk = (2 * t < nv ? 0x0000FFFFu : 0u) | (2 * t + 1 < nv ? 0xFFFF0000u : 0u);
-        const uint32_t hb = st_s + h * HS;
-#pragma unroll
-        for (int mb = 0; mb < KB; ++mb) {
-          ldsm_x2_t(va[h][mb][0], va[h][mb][1], hb + 16 * D + r * (2 * D) + (((2 * mb + sel) ^ r) * 16));
-          va[h][mb][0] &= msk;
-          va[h][mb][1] &= msk;
-        }
-      };
-      if constexpr (FP) {
-        const int r = lane & 7, sel = (lane >> 3) & 1, un = lane >> 4;
-        const uint32_t rb = st_s + un * HS + 16 * D + r * (2 * D);
-#pragma unroll
-        for (int mb = 0; mb < KB; ++mb)
-          ldsm_x4_t(va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], rb + (((2 * mb + sel) ^ r) * 16));
-      } else if constexpr (I4) {
-        v_int4(0);
-        v_int4(1);
-      } else {
-        if (kA == 2) v_int4(0); else v_fp_half(0, vA);
-        if (kB == 2) v_int4(1); else v_fp_half(1, vB);
-      }
-
-    // ---- softmax (log2 domain), rescaling only when a score passes the
-    //      running max by more than 2^kThresh ----
-    const bool v = (I4 || FP) ? true : (g < (my_unit ? vB : vA));
-    const float sc0 = v ? (my_unit ? sacc[2] : sacc[0]) * p.scale_log2 : -INFINITY;
-    const float sc1 = v ? (my_unit ? sacc[3] : sacc[1]) * p.scale_log2 : -INFINITY;
-    if (__any_sync(0xffffffffu, sc0 > m_run[0] + kThresh || sc1 > m_run[1] + kThresh)) {
-      float mx0 = sc0, mx1 = sc1;
-#pragma unroll
-      for (int off = 2; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-      }
-      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-      const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m_run[0] - mn0);
-      const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m_run[1] - mn1);
-      l_run[0] *= al0;
-      l_run[1] *= al1;
-#pragma unroll
-      for (int mb = 0; mb < KB; ++mb) {
-        o[mb][0] *= al0; o[mb][1] *= al1;
-        o[mb][2] *= al0; o[mb][3] *= al1;
-      }
-      m_run[0] = mn0;
-      m_run[1] = mn1;
-    }
-    const float pr0 = v ? exp2f(sc0 - m_run[0]) : 0.f;
-    const float pr1 = v ? exp2f(sc1 - m_run[1]) : 0.f;
-    l_run[0] += pr0;
-    l_run[1] += pr1;
-    // ---- O^T += V^T P ----
-    const float xa = my_unit == 0 ? pr0 : 0.f, xb = my_unit == 0 ? pr1 : 0.f;
-    const float ya = my_unit == 1 ? pr0 : 0.f, yb = my_unit == 1 ? pr1 : 0.f;
-    const uint32_t pb0 = movm_t((I4 || (kBF && clsA == 1)) ? H::pack(xa, xb) : O::pack(xa, xb));
-    const uint32_t pb1 = movm_t((I4 || (kBF && clsB == 1)) ? H::pack(ya, yb) : O::pack(ya, yb));
-    {
-      if (uniform) {
-#pragma unroll
-        for (int mb = 0; mb < KB; ++mb) {
-          if (I4 || use_h)
-            H::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
-          else
-            O::mma(o[mb], va[0][mb][0], va[0][mb][1], va[1][mb][0], va[1][mb][1], pb0, pb1);
-        }
-      } else {
-        const uint32_t n0 = clsA == 0 ? 0xFFFFFFFFu : 0u, n1 = clsB == 0 ? 0xFFFFFFFFu : 0u;
-#pragma unroll
-        for (int mb = 0; mb < KB; ++mb) {
-          O::mma(o[mb], va[0][mb][0] & n0, va[0][mb][1] & n0, va[1][mb][0] & n1, va[1][mb][1] & n1,
-                 pb0 & n0, pb1 & n1);
-          H::mma(o[mb], va[0][mb][0] & ~n0, va[0][mb][1] & ~n0, va[1][mb][0] & ~n1, va[1][mb][1] & ~n1,
-                 pb0 & ~n0, pb1 & ~n1);
-        }
-      }
-    }
-    {  // window mass of each unit: sum over its 8 rows (exact fp32)
-      float ms0 = pr0, ms1 = pr1;
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        ms0 += __shfl_xor_sync(0xffffffffu, ms0, off);
-        ms1 += __shfl_xor_sync(0xffffffffu, ms1, off);
-      }
-      if (lane < 4) {
-        float* ms = mass_s + i * 12;
-        ms[my_unit * 4 + hh0] = ms0;
-        ms[my_unit * 4 + hh0 + 1] = ms1;
-        if (my_unit == 0) { ms[8 + hh0] = m_run[0]; ms[8 + hh0 + 1] = m_run[1]; }
-      }
-    }
-
-    __syncwarp();
+    rq_pos = -1;
   };
 
-  // A warp's tiles form a few homogeneous runs (sinks, int4 pages, fp rows,
-  // boundaries).  Each run streams through the ring with its own geometry:
-  // int4 tiles are small (two pages), so their runs keep many more tiles in
-  // flight; the ring drains between runs.
-  auto run_segment = [&](auto mode_c, auto slots_c, int i0, int i1) {
-    constexpr int MODE = decltype(mode_c)::value;
-    constexpr int SLOTS = decltype(slots_c)::value;
-    constexpr int HS = MODE == 1 ? C::kPageBytes : C::kHalfBytes;
-    constexpr int SLOT_BYTES = 2 * HS;
-    static_assert(SLOTS * SLOT_BYTES <= C::kStages * C::kStageBytes, "ring");
-#pragma unroll
-    for (int k = 0; k < SLOTS - 1; ++k) {
-      if (i0 + k < i1) {
-        const int ua = u0 + 2 * (warp + kWarps * (i0 + k));
-        unsigned char* sl = ring + k * SLOT_BYTES;
-        issue_unit(ua, sl);
-        issue_unit(ua + 1, sl + HS);
-      }
-      cp_commit();
-    }
-    int slot = 0, nslot = SLOTS - 1;
-    for (int i = i0; i < i1; ++i) {
-      if (i + SLOTS - 1 < i1) {
-        const int ua_n = u0 + 2 * (warp + kWarps * (i + SLOTS - 1));
-        unsigned char* sl = ring + nslot * SLOT_BYTES;
-        issue_unit(ua_n, sl);
-        issue_unit(ua_n + 1, sl + HS);
-      }
-      cp_commit();
-      nslot = nslot + 1 == SLOTS ? 0 : nslot + 1;
-      const int ua = u0 + 2 * (warp + kWarps * i);
-      const int kA = MODE == 1 ? 2 : (MODE == 2 ? 1 : R.kind(ua));
-      const int kB = MODE == 1 ? 2 : (MODE == 2 ? 1 : R.kind(ua + 1));
-      const int vA = MODE != 0 ? 8 : (kA == 2 ? 8 : (kA == 1 ? fp_valid(p, R, ua) : 0));
-      const int vB = MODE != 0 ? 8 : (kB == 2 ? 8 : (kB == 1 ? fp_valid(p, R, ua + 1) : 0));
-      tile(mode_c, slots_c, i, ua, kA, kB, vA, vB, ring + slot * SLOT_BYTES);
-      slot = slot + 1 == SLOTS ? 0 : slot + 1;
-    }
-  };
-  auto tile_mode = [&](int i) -> int {
-    const int ua = u0 + 2 * (warp + kWarps * i);
-    const int kA = R.kind(ua), kB = R.kind(ua + 1);
-    if (kA == 2 && kB == 2) return 1;
-    if (kA == 1 && kB == 1 && fp_valid(p, R, ua) == 8 && fp_valid(p, R, ua + 1) == 8) return 2;
-    return 0;
-  };
-  constexpr int kI4Slots = (int)(C::kStages * C::kStageBytes / (2 * C::kPageBytes)) < 8
-                               ? (int)(C::kStages * C::kStageBytes / (2 * C::kPageBytes))
-                               : 8;
-  for (int i = 0; i < my_tiles;) {
-    const int m = tile_mode(i);
-    int j = i + 1;
-    while (j < my_tiles && tile_mode(j) == m) ++j;
-    if (m == 1)
-      run_segment(std::integral_constant<int, 1>{}, std::integral_constant<int, kI4Slots>{}, i, j);
-    else if (m == 2)
-      run_segment(std::integral_constant<int, 2>{}, std::integral_constant<int, C::kStages>{}, i, j);
-    else
-      run_segment(std::integral_constant<int, 0>{}, std::integral_constant<int, C::kStages>{}, i, j);
-    i = j;
+  // ---- this warp's run: generic | int4 | generic | fp | generic ----
+  {
+    const int a = max(tb, min(tr.ia, te)), bi = max(a, min(tr.ib, te));
+    const int f = max(bi, min(tr.fa, te)), fe = max(f, min(tr.fb, te));
+    if (tb < a) run_generic(tb, a);
+    if (a < bi) run_int4(a, bi);
+    if (bi < f) run_generic(bi, f);
+    if (f < fe) run_fp(f, fe);
+    if (fe < te) run_generic(fe, te);
   }
   cp_wait<0>();
 
@@ -585,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
 #pragma unroll
     for (int c = 0; c < 4; ++c) o[mb][c] += __shfl_xor_sync(0xffffffffu, o[mb][c], 2);
 
-  __syncthreads();  // ring and table are free: reuse them for the CTA merge
+  __syncthreads();  // rings are free: reuse them for the CTA merge
   float* wm = reinterpret_cast<float*>(smem);       // [kWarps][4]
   float* wl = wm + kWarps * 4;                      // [kWarps][4]
   float* wo = wl + kWarps * 4;                      // [kWarps][4][D]
@@ -605,14 +748,14 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
     }
   }
   __syncthreads();
-  __shared__ float s_M[4];
+  float* s_M = wo + kWarps * 4 * D;                 // [4]
   if (threadIdx.x < 4) {
     float M = -INFINITY;
     for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w * 4 + threadIdx.x]);
     s_M[threadIdx.x] = M;
   }
   __syncthreads();
-  float* part = p.part + (((int64_t)b * p.Hkv + kh) * p.n_split + split) * 4 * (D + 2);
+  // CTA partial per head: O and sum relative to the CTA max, and the max
   for (int e = threadIdx.x; e < 4 * (D + 2); e += kThreads) {
     const int hh = e / (D + 2), c = e % (D + 2);
     const float M = s_M[hh];
@@ -623,109 +766,167 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       for (int w = 0; w < kWarps; ++w) {
         const float mw = wm[w * 4 + hh];
         if (mw == -INFINITY) continue;
-        acc += exp2f(mw - M) * (c == D + 1 ? wl[w * 4 + hh] : wo[(w * 4 + hh) * D + c]);
+        acc += ex2(mw - M) * (c == D + 1 ? wl[w * 4 + hh] : wo[(w * 4 + hh) * D + c]);
       }
     }
-    part[e] = acc;
+    p.part[(((int64_t)b * p.Hkv + kh) * p.n_split + split) * 4 * (D + 2) + e] = acc;
   }
-  // window masses of this warp's units, relative to the CTA max
-  const float* msw = reinterpret_cast<const float*>(smem + C::kRingBytes) + warp * kMaxTilesPerWarp * 12;
-  for (int e = lane; e < my_tiles * 8; e += 32) {
-    const int i = e >> 3, h = (e >> 2) & 1, hh = e & 3;
-    const int u = u0 + 2 * (warp + kWarps * i) + h;
-    if (u >= u1 || u < p.NS) continue;
-    const float mt = msw[i * 12 + 8 + hh];
-    const float val = (mt == -INFINITY) ? 0.f : msw[i * 12 + h * 4 + hh] * exp2f(mt - s_M[hh]);
-    p.mass[((int64_t)b * p.Hkv * 4 + kh * 4 + hh) * p.W + (u - p.NS)] = val;
+  const int n_units = u1 - u0;
+  {
+    // window masses of the CTA's units, relative to the CTA max
+    for (int e = threadIdx.x; e < 4 * n_units; e += kThreads) {
+      const int hh = e / n_units, k = e - hh * n_units;
+      const int u = u0 + k;
+      if (u < R.NS) continue;
+      const int i = k >> 1, h = k & 1;
+      const float mt = mass_s[i * 12 + 8 + hh];
+      const float val = (mt == -INFINITY) ? 0.f : mass_s[i * 12 + h * 4 + hh] * ex2(mt - s_M[hh]);
+      p.mass[((int64_t)b * p.Hkv * 4 + kh * 4 + hh) * p.W + (u - R.NS)] = val;
+    }
   }
 }
 
-// Combine the splits of one (row, query head): blockIdx.x == 0 writes the
-// output, every block adds the normalised mass of its window chunk.
-constexpr int kMergeThreads = 128;
-constexpr int kMergeWindows = 4 * kMergeThreads;  // windows per block
+// Combine the splits of one (row, kv head) for its 4 query heads: the block
+// with blockIdx.x == 0 writes the output, every block adds the normalised
+// mass of its window chunk.  It is launched as a programmatic dependent of
+// the decode kernel: its blocks start while the decode's last blocks run,
+// load the score accumulator (which the decode does not touch), then wait for
+// the decode grid before reading its partials and masses.
+constexpr int kMergeThreads = 256;
+constexpr int kMergePer = 2;                               // windows per thread and head
+constexpr int kMergeWindows = kMergePer * kMergeThreads;   // windows per block
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const __grid_constant__ MmaParams p) {
-  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int kh = h >> 2, hh = h & 3;
+  const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int Hq = p.Hkv * 4;
-  __shared__ float s_f[kMaxSplits];
-  __shared__ float s_invL;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float s_f[4][kMaxSplits];   // split factor / L per head
+  __shared__ int s_bnd[kMaxSplits + 1];
+  const int w0 = chunk * kMergeWindows, w_end = min(p.W, w0 + kMergeWindows);
+  float* acc = p.scores ? p.scores + ((int64_t)b * Hq + kh * 4) * p.scores_cap : nullptr;
+  float av[4][kMergePer];
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh)
+#pragma unroll
+    for (int k = 0; k < kMergePer; ++k) {
+      const int w = w0 + threadIdx.x + k * kMergeThreads;
+      av[hh][k] = (acc && w < w_end) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
+    }
+  for (int j = threadIdx.x; j <= p.n_split; j += kMergeThreads) s_bnd[j] = p.bnd[j];
+  grid_dependency_wait();
   const float* part = p.part + ((int64_t)b * p.Hkv + kh) * p.n_split * 4 * (D + 2);
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    float ms[2], ls[2];
+  const float* ms = p.mass + ((int64_t)b * Hq + kh * 4) * p.W;
+  float mv[4][kMergePer];
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh)
+#pragma unroll
+    for (int k = 0; k < kMergePer; ++k) {
+      const int w = w0 + threadIdx.x + k * kMergeThreads;
+      mv[hh][k] = (acc && w < w_end) ? ms[(int64_t)hh * p.W + w] : 0.f;
+    }
+  // output partials of the first splits, loaded before the statistics exist
+  constexpr int kOut = 4 * D / kMergeThreads;  // (head, channel) pairs per thread
+  constexpr int kPre = 16;                     // splits prefetched per pair
+  float ov[kOut][kPre];
+  if (chunk == 0) {
+#pragma unroll
+    for (int q = 0; q < kOut; ++q) {
+      const int e = threadIdx.x + q * kMergeThreads, hh = e / D, c = e - hh * D;
+#pragma unroll
+      for (int sp = 0; sp < kPre; ++sp) ov[q][sp] = sp < p.n_split ? part[(sp * 4 + hh) * (D + 2) + c] : 0.f;
+    }
+  }
+  if (warp < 4) {  // warp hh: the split statistics of head hh
+    const int hh = warp;
+    float m2[2], l2[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      const int s = lane + 32 * k;
-      ms[k] = s < p.n_split ? part[(s * 4 + hh) * (D + 2) + D] : -INFINITY;
-      ls[k] = s < p.n_split ? part[(s * 4 + hh) * (D + 2) + D + 1] : 0.f;
+      const int sp = lane + 32 * k;
+      m2[k] = sp < p.n_split ? part[(sp * 4 + hh) * (D + 2) + D] : -INFINITY;
+      l2[k] = sp < p.n_split ? part[(sp * 4 + hh) * (D + 2) + D + 1] : 0.f;
     }
-    const float M = warp_max(fmaxf(ms[0], ms[1]));
-    float L = 0.f;
+    const float M = warp_max(fmaxf(m2[0], m2[1]));
+    float f2[2], L = 0.f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      const float f = ms[k] == -INFINITY ? 0.f : exp2f(ms[k] - M);
-      if (lane + 32 * k < p.n_split) s_f[lane + 32 * k] = f;
-      L += f * ls[k];
+      f2[k] = m2[k] == -INFINITY ? 0.f : exp2f(m2[k] - M);
+      L += f2[k] * l2[k];
     }
-    L = warp_sum(L);
-    if (lane == 0) s_invL = 1.f / L;
+    const float invL = 1.f / warp_sum(L);
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (lane + 32 * k < p.n_split) s_f[hh][lane + 32 * k] = f2[k] * invL;
   }
   __syncthreads();
-  const float invL = s_invL;
   if (chunk == 0) {
-    for (int c = threadIdx.x; c < D; c += blockDim.x) {
-      float acc = 0.f;
-      for (int s = 0; s < p.n_split; ++s) acc += s_f[s] * part[(s * 4 + hh) * (D + 2) + c];
-      st_f32((T*)p.out + b * p.o_sb + h * p.o_sh + c, acc * invL);
+#pragma unroll
+    for (int q = 0; q < kOut; ++q) {
+      const int e = threadIdx.x + q * kMergeThreads, hh = e / D, c = e - hh * D;
+      float o = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < kPre; ++sp) o += s_f[hh][sp < p.n_split ? sp : 0] * ov[q][sp];
+#pragma unroll 8
+      for (int sp = kPre; sp < p.n_split; ++sp) o += s_f[hh][sp] * part[(sp * 4 + hh) * (D + 2) + c];
+      st_f32((T*)p.out + b * p.o_sb + (kh * 4 + hh) * p.o_sh + c, o);
     }
   }
-  if (p.scores == nullptr) return;
-  const float* __restrict__ ms = p.mass + ((int64_t)b * Hq + h) * p.W;
-  float* __restrict__ acc = p.scores + ((int64_t)b * Hq + h) * p.scores_cap;
-  const int w_end = min(p.W, (chunk + 1) * kMergeWindows);
-  float mv[4], av[4];
-  int ws[4];
+  if (acc == nullptr) return;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {  // issue all loads first
-    ws[k] = chunk * kMergeWindows + threadIdx.x + k * kMergeThreads;
-    mv[k] = ws[k] < w_end ? ms[ws[k]] : 0.f;
-    av[k] = ws[k] < w_end ? acc[ws[k]] : 0.f;
-  }
+  for (int k = 0; k < kMergePer; ++k) {
+    const int w = w0 + threadIdx.x + k * kMergeThreads;
+    if (w >= w_end) continue;
+    const int u = p.NS + w;
+    int lo = 0, hi = p.n_split - 1;  // last split with bnd <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_bnd[mid] <= u) lo = mid; else hi = mid - 1;
+    }
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    if (ws[k] >= w_end) continue;
-    const int u = p.NS + ws[k];
-    int sp = 0;
-#pragma unroll 1
-    for (int step = 32; step > 0; step >>= 1)  // last split with bnd <= u
-      if (sp + step < p.n_split && p.bnd[sp + step] <= u) sp += step;
-    acc[ws[k]] = av[k] + mv[k] * s_f[sp] * invL;
+    for (int hh = 0; hh < 4; ++hh) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
   }
 }
 
 template <int D>
 void plan_splits(MmaParams& p) {
-  // Every 16-token tile costs about the same time whether it holds fp or int4
-  // units (the kernel is bound by per-tile latency, not bytes), so ranges
-  // hold equal unit counts; the split count fills whole waves of resident CTAs.
+  // Ranges hold equal estimated cost (the per-tile costs of the kernel's
+  // tile classes); the split count fills whole waves of resident CTAs.
+  const int TB = p.NS + p.n_tp, UF = TB + p.rest / 8;
+  auto clampi = [](int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); };
+  // cost of units [0, u), in half-tile units (2x the per-tile cost per pair)
+  auto prefix = [&](int u) -> int64_t {
+    return (int64_t)kCostGeneric * clampi(u, 0, p.NS) + (int64_t)kCostI4 * clampi(u - p.NS, 0, p.n_tp) +
+           (int64_t)kCostFp * clampi(u - TB, 0, UF - TB) + (int64_t)kCostGeneric * max(0, u - UF);
+  };
   const int units = p.B * p.Hkv;
   const int slots = 148 * (D == 64 ? 4 : 2);
   int n = max(1, (2 * slots) / max(1, units));
   n = max(n, ceil_div(p.U, kMaxUnitsPerSplit));
   n = min(n, kMaxSplits);
   n = min(n, max(1, p.U / 16));
-  int per = ceil_div(p.U, n);
-  per = (per + 1) & ~1;
+  const int64_t total = prefix(p.U);
   p.bnd[0] = 0;
   int k = 1;
   while (p.bnd[k - 1] < p.U && k <= kMaxSplits) {
-    p.bnd[k] = min(p.U, p.bnd[k - 1] + per);
+    const int64_t target = total * k / n;
+    int lo = p.bnd[k - 1] + 1, hi = p.U;  // smallest u with prefix(u) >= target
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix(mid) >= target) hi = mid; else lo = mid + 1;
+    }
+    int e = (lo + 1) & ~1;
+    e = max(e, p.bnd[k - 1] + 2);
+    e = min(e, p.bnd[k - 1] + kMaxUnitsPerSplit);
+    p.bnd[k] = min(e, p.U);
     ++k;
   }
   p.n_split = k - 1;
+  if (p.bnd[p.n_split] != p.U) {  // caps left units over: fall back to equal unit counts
+    n = max(ceil_div(p.U, kMaxUnitsPerSplit), min(n, kMaxSplits));
+    const int per = (ceil_div(p.U, n) + 1) & ~1;
+    p.n_split = ceil_div(p.U, per);
+    for (int j = 0; j <= p.n_split; ++j) p.bnd[j] = min(p.U, j * per);
+  }
 }
 
 template <typename T, int D>
@@ -733,12 +934,23 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
   using C = Cfg<D>;
   static_assert(C::kSmemBytes <= 227 * 1024, "smem");
   cudaFuncSetAttribute(decode_mma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmemBytes);
-  dim3 grid(p.n_split, p.Hkv, p.B);
-  decode_mma_kernel<T, D><<<grid, kThreads, C::kSmemBytes, stream>>>(p);
+  decode_mma_kernel<T, D><<<dim3(p.n_split, p.Hkv, p.B), kThreads, C::kSmemBytes, stream>>>(p);
   SKV_CHECK_LAUNCH();
-  const int chunks = p.scores ? max(1, ceil_div(p.W, kMergeWindows)) : 1;
-  decode_mma_merge_kernel<T, D><<<dim3(chunks, p.Hkv * 4, p.B), kMergeThreads, 0, stream>>>(p);
-  SKV_CHECK_LAUNCH();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.scores ? max(1, ceil_div(p.W, kMergeWindows)) : 1, p.Hkv, p.B);
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_mma_merge_kernel<T, D>, p);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return SKV_ERR_CUDA;
+  }
   return SKV_OK;
 }
 
@@ -760,6 +972,11 @@ bool decode_mma_supported(const skv_layer_desc* L) {
   return (L->kv_dtype == SKV_F16 || L->kv_dtype == SKV_BF16) && (L->head_dim == 64 || L->head_dim == 128) &&
          L->num_q_heads == 4 * L->num_kv_heads && L->window_size == kPageTokens && L->fp_capacity % 8 == 0;
 }
+
+// Lengths the split plan covers: at least one full tile, at most
+// kMaxSplits ranges of kMaxUnitsPerSplit units (the sink unit, a partial
+// unit and the 8-token units in between).
+bool decode_mma_length_ok(int T) { return T >= 16 && (int64_t)T / kPageTokens + 2 <= (int64_t)kMaxSplits * kMaxUnitsPerSplit; }
 
 size_t decode_mma_ws_size(const skv_layer_desc* L, int T) { return mma_ws(L, T).total; }
 

@@ -12,6 +12,30 @@ from oracle import skv_oracle as O
 TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 # Attention-output tolerance per KV dtype (max-abs vs the fp32 eager restatement).
 OUT_TOL = {"f32": 2e-5, "f16": 2e-3, "bf16": 8e-3}
+_MANT_BITS = {"f16": 10, "bf16": 7}
+
+
+def assert_out_close(actual, desired, dt: str, err_msg: str = "") -> None:
+    """Attention output against the oracle's fp32 output.
+
+    The reference's eager path returns the model dtype, so the oracle output
+    is rounded to the KV dtype first.  The two must then agree within the
+    max-abs tolerance OUT_TOL[dt] (2e-3 fp16, 8e-3 bf16, 2e-5 fp32), or within
+    one unit in the last place of the dtype where that unit is larger (bf16
+    values of magnitude >= 2, fp16 >= 4): two correctly rounded results of
+    sums that differ only in summation order can land one ulp apart."""
+    a = np.asarray(actual, dtype=np.float32)
+    d = O.round_to(np.asarray(desired, dtype=np.float32), dt)
+    tol = np.full(d.shape, OUT_TOL[dt], dtype=np.float32)
+    if dt in _MANT_BITS:
+        mag = np.maximum(np.abs(d), np.float32(1e-30))
+        ulp = np.exp2(np.floor(np.log2(mag)) - _MANT_BITS[dt]).astype(np.float32)
+        tol = np.maximum(tol, ulp)
+    bad = ~(np.abs(a - d) <= tol)
+    if bad.any():
+        i = np.unravel_index(np.argmax(np.where(bad, np.abs(a - d) - tol, -np.inf)), a.shape)
+        raise AssertionError(f"{err_msg}: {int(bad.sum())}/{a.size} outside tolerance; worst at {i}: "
+                             f"actual {a[i]!r} desired {d[i]!r} tol {tol[i]!r}")
 
 
 @dataclass
