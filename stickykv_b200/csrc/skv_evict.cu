@@ -12,14 +12,15 @@
 // and adds the demotion of kept windows into the int4 tier (design.md:130-187).
 //
 // Kernel 1 (select): one CTA per row.  Head-mean of the window scores, exact
-// top-k by a radix select on 64-bit keys (score bits, then inverted window
-// index so the lowest index wins ties), chronological compaction, the
-// score/id gather and, with the tier, the new page table.
-// Kernel 2 (move): fp tokens that stay fp are copied to the destination store
-// with their keys stripped at the old and re-applied at the new position,
-// op by op in the KV dtype like the reference.
-// Kernel 3 (demote): kept fp windows entering the tier are rotated into their
-// page frame and quantised to int4 pages, one warp per page.
+// top-k by a radix select on the orderable score bits (the lowest window
+// index wins ties: among keys equal to the threshold the first ones in window
+// order are kept), chronological compaction and, with the tier, the new page
+// table.
+// Kernel 2 (apply): the fp tokens that stay fp are copied to the destination
+// store with their keys stripped at the old and re-applied at the new
+// position, op by op in the KV dtype like the reference; kept fp windows
+// entering the tier are rotated into their page frame and quantised to int4
+// pages (a block per page); scores and ids are gathered.
 #include <float.h>
 
 #include "skv_common.cuh"
@@ -71,38 +72,39 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int b = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);                 // [E]
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                   // [E]
   int* hist = reinterpret_cast<int*>(keys + (p.E > 0 ? p.E : 1));           // [256]
   int* scan = hist + 256;                                                   // [32]
   int* ret = scan + 32;                                                     // [R]
   int* free_list = ret + (p.R > 0 ? p.R : 1);                               // [page_cap]
   unsigned char* used = reinterpret_cast<unsigned char*>(free_list + (p.tier ? p.page_cap : 0));
-  __shared__ uint64_t s_thr;
+  __shared__ uint32_t s_digit;
   __shared__ int s_krem;
 
   const int E = p.E, k = p.kprime;
-  // 1. head-mean keys over the evictable prefix
-  if (k > 0 && k < E) {
+  const bool partial = k > 0 && k < E;
+  // 1. head-mean keys over the evictable prefix (orderable float bits)
+  uint32_t thr = 0;
+  int krem = 0;  // keys equal to thr that are kept, lowest window index first
+  if (partial) {
     for (int w = tid; w < E; w += nt) {
       float acc = 0.f;
       for (int h = 0; h < p.Hq; ++h) acc = __fadd_rn(acc, p.scores_src[((int64_t)b * p.Hq + h) * p.scores_cap + w]);
-      const float mean = __fdiv_rn(acc, (float)p.Hq);
-      keys[w] = ((uint64_t)orderable(mean) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)w);
+      keys[w] = orderable(__fdiv_rn(acc, (float)p.Hq));
     }
-    __syncthreads();
-    // 2. radix select of the k-th largest key (keys are unique)
-    uint64_t prefix = 0, pmask = 0;
     if (tid == 0) s_krem = k;
-    for (int shift = 56; shift >= 0; shift -= 8) {
+    // 2. radix select of the k-th largest key, 8 bits per pass
+    uint32_t prefix = 0, pmask = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
       for (int i = tid; i < 256; i += nt) hist[i] = 0;
       __syncthreads();
       for (int w = tid; w < E; w += nt) {
-        const uint64_t key = keys[w];
+        const uint32_t key = keys[w];
         if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
       }
       __syncthreads();
       if (tid < 32) {  // one warp finds the digit holding the krem-th largest key
-        const int krem = s_krem;
+        const int kr = s_krem;
         int cnt[8], tot = 0;
 #pragma unroll
         for (int q = 0; q < 8; ++q) { cnt[q] = hist[255 - (tid * 8 + q)]; tot += cnt[q]; }
@@ -113,14 +115,14 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
           if (tid >= o) incl += y;
         }
         const int excl = incl - tot;
-        const unsigned own = __ballot_sync(0xffffffffu, excl < krem && krem <= incl);
+        const unsigned own = __ballot_sync(0xffffffffu, excl < kr && kr <= incl);
         if (tid == __ffs(own) - 1) {
           int c = excl;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            if (c + cnt[q] >= krem) {
-              s_thr = (uint64_t)(255 - (tid * 8 + q));
-              s_krem = krem - c;
+            if (c + cnt[q] >= kr) {
+              s_digit = (uint32_t)(255 - (tid * 8 + q));
+              s_krem = kr - c;
               break;
             }
             c += cnt[q];
@@ -128,31 +130,43 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
         }
       }
       __syncthreads();
-      prefix |= s_thr << shift;
-      pmask |= (uint64_t)255 << shift;
-      __syncthreads();
+      prefix |= s_digit << shift;
+      pmask |= 255u << shift;
     }
-    if (tid == 0) s_thr = prefix;
-    __syncthreads();
+    thr = prefix;
+    krem = s_krem;
   }
-  // 3. chronological positions of the kept evictable windows
+  // 3. chronological positions of the kept evictable windows: keys above the
+  //    threshold, and the first krem windows whose key equals it
   const int per = (E + nt - 1) / nt;
   const int w0 = tid * per, w1 = min(E, w0 + per);
-  const uint64_t thr = (k > 0 && k < E) ? s_thr : 0;
-  auto kept = [&](int w) -> bool {
+  int n_eq = 0;
+  if (partial)
+    for (int w = w0; w < w1; ++w) n_eq += keys[w] == thr ? 1 : 0;
+  int eq_total = 0;
+  int eq_rank = block_excl_scan(n_eq, scan, eq_total);
+  auto kept = [&](int w, int& rank) -> bool {
     if (k == 0) return false;
     if (k >= E) return true;
-    return keys[w] >= thr;
+    const uint32_t key = keys[w];
+    if (key != thr) return key > thr;
+    return rank++ < krem;
   };
   int cnt = 0;
-  for (int w = w0; w < w1; ++w) cnt += kept(w) ? 1 : 0;
+  {
+    int r = eq_rank;
+    for (int w = w0; w < w1; ++w) cnt += kept(w, r) ? 1 : 0;
+  }
   int total = 0;
   int pos = block_excl_scan(cnt, scan, total);
-  for (int w = w0; w < w1; ++w)
-    if (kept(w)) ret[pos++] = w;
+  {
+    int r = eq_rank;
+    for (int w = w0; w < w1; ++w)
+      if (kept(w, r)) ret[pos++] = w;
+  }
   for (int i = tid; i < p.local_w; i += nt) ret[k + i] = E + i;
   __syncthreads();
-  // 4. retained list (the score/id gather runs in evict_gather_kernel)
+  // 4. retained list (the score/id gather runs in the apply kernel)
   for (int j = tid; j < p.R; j += nt) {
     p.retained[(int64_t)b * p.R + j] = ret[j];
     if (p.retained_out) p.retained_out[(int64_t)b * p.scores_cap + j] = ret[j];
@@ -205,37 +219,178 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   }
 }
 
-// Score and original-id gather (cache.py:271-283), one CTA per (query head,
-// row); windows that appear before the next eviction start at zero score and
-// take ids from the running counter (cache.py:180-213).
-__global__ void __launch_bounds__(256) evict_gather_kernel(EvictParams p) {
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int* __restrict__ ret = p.retained + (int64_t)b * p.R;
-  const float* __restrict__ src = p.scores_src + ((int64_t)b * p.Hq + h) * p.scores_cap;
-  float* __restrict__ dst = p.scores_dst + ((int64_t)b * p.Hq + h) * p.scores_cap;
-  const int ztail = min(p.scores_cap - p.R, kTailWindows);
-#pragma unroll 4
-  for (int j = threadIdx.x; j < p.R + ztail; j += blockDim.x) dst[j] = j < p.R ? src[ret[j]] : 0.f;
-  if (h == 0) {
-    const int64_t* __restrict__ is = p.ids_src + (int64_t)b * p.scores_cap;
-    int64_t* __restrict__ id = p.ids_dst + (int64_t)b * p.scores_cap;
-#pragma unroll 4
-    for (int j = threadIdx.x; j < p.R + ztail; j += blockDim.x)
-      id[j] = j < p.R ? is[ret[j]] : p.next_window_id + (j - p.R);
+// ---------------------------------------------------------------------------
+// Kernel 2 (apply): one launch for everything that follows the selection.
+// Blocks [0, n_demote) quantise entrant windows into int4 pages, blocks
+// [n_demote, +n_gather) gather scores and ids, the rest move the fp tokens
+// that stay fp.  The three write disjoint buffers and read only the source
+// side and the selection, so they run side by side; the short demotion and
+// gather blocks come first in the grid so they overlap the long move.
+// ---------------------------------------------------------------------------
+constexpr int kApplyThreads = 256;
+
+// Quantise one 8-token page (keys rotated to the page frame) and pack it,
+// with the whole block.  `kin(r, c)` / `vin(r, c)` give token r channel c as
+// fp32; `pos0` is the logical position of row 0.  The page is staged in
+// shared memory as fp32; each (K or V, row, 32-channel group) is quantised
+// by kApplyThreads / (16 * D / 32) threads that reduce min/max by shuffles.
+// Scratch: 2*8*D floats + 2*8*D code bytes.
+template <int D, typename KF, typename VF>
+__device__ void quantize_page_block(KF kin, VF vin, int pos0, const float* cos, const float* sin,
+                                    uint8_t* page, unsigned char* scratch) {
+  constexpr int half = D / 2, ng = D / kQGroup;
+  constexpr int kTasks = 2 * 8 * ng;                 // (K|V, row, group)
+  constexpr int kTPT = kApplyThreads / kTasks;       // threads per task
+  constexpr int kEPT = kQGroup / kTPT;               // elements per thread
+  static_assert(kTPT >= 1 && kTPT <= 32 && (32 % kTPT) == 0 && kEPT * kTPT == kQGroup, "task split");
+  const int tid = threadIdx.x;
+  float* kf = reinterpret_cast<float*>(scratch);
+  float* vf = kf + 8 * D;
+  uint8_t* kc = reinterpret_cast<uint8_t*>(vf + 8 * D);
+  uint8_t* vc = kc + 8 * D;
+  for (int idx = tid; idx < 8 * half; idx += kApplyThreads) {
+    const int r = idx / half, cp = idx % half;
+    float x = kin(r, cp), y = kin(r, cp + half);
+    const int64_t pos = pos0 + r;
+    to_page_frame(x, y, cos[pos * half + cp], sin[pos * half + cp], cos[(int64_t)r * half + cp],
+                  sin[(int64_t)r * half + cp]);
+    kf[r * D + cp] = x;
+    kf[r * D + cp + half] = y;
+  }
+  for (int idx = tid; idx < 8 * D; idx += kApplyThreads) vf[idx] = vin(idx / D, idx % D);
+  __syncthreads();
+  {
+    const int task = tid / kTPT, sub = tid % kTPT;
+    const int which = task / (8 * ng);  // 0 = K, 1 = V
+    const int r = (task / ng) % 8, gq = task % ng;
+    const float* src = (which ? vf : kf) + r * D + gq * kQGroup + sub * kEPT;
+    float xv[kEPT];
+    float mn = FLT_MAX, mx = -FLT_MAX;
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) {
+      xv[e] = src[e];
+      mn = fminf(mn, xv[e]);
+      mx = fmaxf(mx, xv[e]);
+    }
+#pragma unroll
+    for (int o = 1; o < kTPT; o <<= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const __half s16 = __float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), 15.f));
+    const __half z16 = __float2half_rn(mn);
+    const float sc = __half2float(s16), z = __half2float(z16);
+    uint8_t* codes = (which ? vc : kc) + r * D + gq * kQGroup + sub * kEPT;
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) {
+      int q = 0;
+      if (sc != 0.f) q = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(xv[e], z), sc)), 0.f), 15.f);
+      codes[e] = (uint8_t)q;
+    }
+    if (sub == 0) {
+      if (which == 0) {
+        __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
+        kscl[(r * ng + gq) * 2] = s16;
+        kscl[(r * ng + gq) * 2 + 1] = z16;
+      } else {
+        __half* e4 = reinterpret_cast<__half*>(page + page_v_scales_off(D)) + ((r >> 1) * ng + gq) * 4;
+        e4[r & 1] = s16;
+        e4[2 + (r & 1)] = z16;
+      }
+    }
+  }
+  __syncthreads();
+  // fragment-order words: K [row][lane t][word], V [pair t][row g][word]
+  for (int idx = tid; idx < 2 * 32 * ng; idx += kApplyThreads) {
+    uint32_t word = 0;
+    if (idx < 32 * ng) {
+      const int r = idx / (4 * ng), t = (idx / ng) % 4, w = idx % ng;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ch = 2 * t + 8 * (4 * w + i);
+        word |= (uint32_t)kc[r * D + ch] << (4 * i);
+        word |= (uint32_t)kc[r * D + ch + 1] << (4 * (i + 4));
+      }
+      reinterpret_cast<uint32_t*>(page)[idx] = word;
+    } else {
+      const int v = idx - 32 * ng;
+      const int t = v / (8 * ng), g = (v / ng) % 8, w = v % ng;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ch = g + 8 * (4 * w + i);
+        word |= (uint32_t)vc[(2 * t) * D + ch] << (4 * i);
+        word |= (uint32_t)vc[(2 * t + 1) * D + ch] << (4 * (i + 4));
+      }
+      reinterpret_cast<uint32_t*>(page + page_v_codes_off(D))[v] = word;
+    }
   }
 }
 
-// Copy fp tokens that stay fp into the destination store, keys re-rotated.
-// One thread per (token, 16-byte vector of the first half of the channels):
-// it handles the vector and its rotation partner in the second half.
-template <typename T>
-__global__ void __launch_bounds__(256) evict_move_kernel(EvictParams p, int n_fp_tok) {
+// shared scratch for quantize_page_block
+__host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D * 4 + 2 * 8 * D; }
+
+struct ApplyGrid {
+  int n_demote, n_gather, n_move;
+  int demote_tasks;   // (candidate window, page) pairs per (row, kv head)
+  int gather_chunks;  // kApplyThreads-window chunks per row
+  int move_chunks;    // token chunks per row
+  int n_fp_tok;       // fp tokens that stay fp, per row
+};
+
+// Demotion: kept fp windows entering the tier are rotated into their page
+// frame and quantised (design.md:130-187).
+template <typename T, int D>
+__device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, unsigned char* smem) {
+  const int task = bid % a.demote_tasks, bh = bid / a.demote_tasks;
+  const int h = bh % p.Hkv, b = bh / p.Hkv;
+  const int n_tw_old = p.n_tier_old_tok / p.ws;
+  const int cand = task / p.ppw, pi = task % p.ppw;
+  const int j = p.entrant[(int64_t)b * p.W + cand];
+  if (j < 0) return;  // candidate window dropped
+  const int w = n_tw_old + cand;
+  const int pos0 = p.s + w * p.ws + pi * kPageTokens;
+  const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
+  const int64_t rb = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + go.fp_slot(pos0)) * D;
+  const T* ks = (const T*)p.k_src + rb;
+  const T* vs = (const T*)p.v_src + rb;
+  const int phys = p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + pi];
+  uint8_t* page = p.pages + (((int64_t)b * p.Hkv + h) * p.page_cap + phys) * page_bytes(D);
+  quantize_page_block<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
+                         [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos, p.sin,
+                         page, smem);
+}
+
+// Score and original-id gather (cache.py:271-283) for one chunk of retained
+// windows of one row, all query heads; windows that appear before the next
+// eviction start at zero score and take ids from the running counter
+// (cache.py:180-213).
+__device__ void gather_block(const EvictParams& p, const ApplyGrid& a, int bid) {
+  const int b = bid / a.gather_chunks, chunk = bid % a.gather_chunks;
+  const int ztail = min(p.scores_cap - p.R, kTailWindows);
+  const int j = chunk * kApplyThreads + threadIdx.x;
+  if (j >= p.R + ztail) return;
+  const int r = j < p.R ? p.retained[(int64_t)b * p.R + j] : -1;
+  const float* src = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
+  float* dst = p.scores_dst + (int64_t)b * p.Hq * p.scores_cap;
+#pragma unroll 8
+  for (int h = 0; h < p.Hq; ++h)
+    dst[(int64_t)h * p.scores_cap + j] = r >= 0 ? src[(int64_t)h * p.scores_cap + r] : 0.f;
+  p.ids_dst[(int64_t)b * p.scores_cap + j] =
+      r >= 0 ? p.ids_src[(int64_t)b * p.scores_cap + r] : p.next_window_id + (j - p.R);
+}
+
+// fp tokens that stay fp, copied into the destination store with their keys
+// stripped at the old and re-applied at the new position (op by op in the
+// KV dtype).  A thread owns one (token, 16-byte vector of the first half of
+// the channels) of one row and walks the KV heads, so its cos/sin rows are
+// loaded once; it handles the vector and its rotation partner.
+template <typename T, int D>
+__device__ void move_block(const EvictParams& p, const ApplyGrid& a, int bid) {
   constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
-  const int b = blockIdx.z, h = blockIdx.y;
-  const int half = p.D / 2, nvec = half / VE;
-  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)n_fp_tok * nvec) return;
-  const int tau = (int)(idx / nvec), c0 = (int)(idx % nvec) * VE;
+  constexpr int half = D / 2, nvec = half / VE, tpb = kApplyThreads / nvec;
+  const int b = bid / a.move_chunks, chunk = bid % a.move_chunks;
+  const int tau = chunk * tpb + threadIdx.x / nvec, c0 = (threadIdx.x % nvec) * VE;
+  if (threadIdx.x >= tpb * nvec || tau >= a.n_fp_tok) return;
   const int s_eff = min(p.s, p.T_old);
   int old_pos, new_pos;
   if (tau < s_eff) {
@@ -250,16 +405,6 @@ __global__ void __launch_bounds__(256) evict_move_kernel(EvictParams p, int n_fp
   }
   const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
   const Geometry gn{p.s, p.s_pad, p.ws, p.T_new, p.n_tier_new_tok};
-  const int64_t rs = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + go.fp_slot(old_pos)) * p.D;
-  const int64_t rd = (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + gn.fp_slot(new_pos)) * p.D;
-  const T* ks = (const T*)p.k_src + rs;
-  const T* vs = (const T*)p.v_src + rs;
-  T* kd = (T*)p.k_dst + rd;
-  T* vd = (T*)p.v_dst + rd;
-  union Vec { uint4 u; T e[VE]; };
-  Vec kx, ky, ox, oy;
-  kx.u = *reinterpret_cast<const uint4*>(ks + c0);
-  ky.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
   float co[VE], so[VE], cn[VE], sn[VE];
 #pragma unroll
   for (int e = 0; e < VE; e += 4) {
@@ -268,157 +413,90 @@ __global__ void __launch_bounds__(256) evict_move_kernel(EvictParams p, int n_fp
     *reinterpret_cast<float4*>(cn + e) = *reinterpret_cast<const float4*>(p.cos + (int64_t)new_pos * half + c0 + e);
     *reinterpret_cast<float4*>(sn + e) = *reinterpret_cast<const float4*>(p.sin + (int64_t)new_pos * half + c0 + e);
   }
+  const int64_t so_slot = go.fp_slot(old_pos), sd_slot = gn.fp_slot(new_pos);
+  union Vec { uint4 u; T e[VE]; };
+#pragma unroll 1
+  for (int h = 0; h < p.Hkv; ++h) {
+    const int64_t rs = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
+    const int64_t rd = (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
+    const T* ks = (const T*)p.k_src + rs;
+    const T* vs = (const T*)p.v_src + rs;
+    T* kd = (T*)p.k_dst + rd;
+    T* vd = (T*)p.v_dst + rd;
+    Vec kx, ky, ox, oy;
+    kx.u = *reinterpret_cast<const uint4*>(ks + c0);
+    ky.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
+    const uint4 v0 = *reinterpret_cast<const uint4*>(vs + c0);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(vs + c0 + half);
 #pragma unroll
-  for (int e = 0; e < VE; ++e) {
-    float x = Elt<T>::to_f32(kx.e[e]), y = Elt<T>::to_f32(ky.e[e]);
-    rope_strip_apply<T>(x, y, co[e], so[e], cn[e], sn[e]);
-    ox.e[e] = Elt<T>::from_f32(x);
-    oy.e[e] = Elt<T>::from_f32(y);
-  }
-  *reinterpret_cast<uint4*>(kd + c0) = ox.u;
-  *reinterpret_cast<uint4*>(kd + c0 + half) = oy.u;
-  *reinterpret_cast<uint4*>(vd + c0) = *reinterpret_cast<const uint4*>(vs + c0);
-  *reinterpret_cast<uint4*>(vd + c0 + half) = *reinterpret_cast<const uint4*>(vs + c0 + half);
-}
-
-// Quantise one 8-token page (keys rotated to the page frame) and pack it.
-// `kin(r, c)` / `vin(r, c)` give token r channel c as fp32; `pos0` is the
-// logical position of row 0 (row r sits at pos0 + r; the page starts at a
-// multiple of 8 past the sinks).  One warp.  The page is first staged in
-// shared memory as fp32 (keys already in the page frame) with independent
-// loads, then each lane quantises one (token, group) of K or V.
-// Scratch: 2*8*D floats + 2*8*D code bytes per warp.
-template <int D, typename KF, typename VF>
-__device__ void quantize_page_warp(KF kin, VF vin, int pos0, const float* cos, const float* sin,
-                                   uint8_t* page, unsigned char* scratch) {
-  const int lane = threadIdx.x & 31;
-  const int half = D / 2, ng = D / kQGroup;
-  float* kf = reinterpret_cast<float*>(scratch);
-  float* vf = kf + 8 * D;
-  uint8_t* kc = reinterpret_cast<uint8_t*>(vf + 8 * D);
-  uint8_t* vc = kc + 8 * D;
-#pragma unroll
-  for (int idx = lane; idx < 8 * half; idx += 32) {
-    const int r = idx / half, cp = idx % half;
-    float x = kin(r, cp), y = kin(r, cp + half);
-    const int64_t pos = pos0 + r;
-    to_page_frame(x, y, cos[pos * half + cp], sin[pos * half + cp], cos[(int64_t)r * half + cp],
-                  sin[(int64_t)r * half + cp]);
-    kf[r * D + cp] = x;
-    kf[r * D + cp + half] = y;
-  }
-#pragma unroll
-  for (int idx = lane; idx < 8 * D; idx += 32) vf[idx] = vin(idx / D, idx % D);
-  __syncwarp();
-  __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
-  __half* vscl = reinterpret_cast<__half*>(page + page_v_scales_off(D));
-  for (int task = lane; task < 2 * 8 * ng; task += 32) {
-    const int which = task / (8 * ng);  // 0 = K, 1 = V
-    const int r = (task / ng) % 8, gq = task % ng;
-    const float* src = (which ? vf : kf) + r * D + gq * kQGroup;
-    float mn = FLT_MAX, mx = -FLT_MAX;
-#pragma unroll 8
-    for (int e = 0; e < kQGroup; ++e) {
-      mn = fminf(mn, src[e]);
-      mx = fmaxf(mx, src[e]);
+    for (int e = 0; e < VE; ++e) {
+      float x = Elt<T>::to_f32(kx.e[e]), y = Elt<T>::to_f32(ky.e[e]);
+      rope_strip_apply<T>(x, y, co[e], so[e], cn[e], sn[e]);
+      ox.e[e] = Elt<T>::from_f32(x);
+      oy.e[e] = Elt<T>::from_f32(y);
     }
-    const __half s16 = __float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), 15.f));
-    const __half z16 = __float2half_rn(mn);
-    const float sc = __half2float(s16), z = __half2float(z16);
-    uint8_t* codes = (which ? vc : kc) + r * D + gq * kQGroup;
-#pragma unroll 8
-    for (int e = 0; e < kQGroup; ++e) {
-      int q = 0;
-      if (sc != 0.f) q = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(src[e], z), sc)), 0.f), 15.f);
-      codes[e] = (uint8_t)q;
-    }
-    if (which == 0) {
-      kscl[(r * ng + gq) * 2] = s16;
-      kscl[(r * ng + gq) * 2 + 1] = z16;
-    } else {
-      __half* e4 = vscl + ((r >> 1) * ng + gq) * 4;
-      e4[r & 1] = s16;
-      e4[2 + (r & 1)] = z16;
-    }
+    *reinterpret_cast<uint4*>(kd + c0) = ox.u;
+    *reinterpret_cast<uint4*>(kd + c0 + half) = oy.u;
+    *reinterpret_cast<uint4*>(vd + c0) = v0;
+    *reinterpret_cast<uint4*>(vd + c0 + half) = v1;
   }
-  __syncwarp();
-  uint32_t* kw = reinterpret_cast<uint32_t*>(page);
-  for (int idx = lane; idx < 8 * 4 * ng; idx += 32) {
-    const int r = idx / (4 * ng), t = (idx / ng) % 4, w = idx % ng;
-    uint32_t word = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int ch = 2 * t + 8 * (4 * w + i);
-      word |= (uint32_t)kc[r * D + ch] << (4 * i);
-      word |= (uint32_t)kc[r * D + ch + 1] << (4 * (i + 4));
-    }
-    kw[idx] = word;
-  }
-  uint32_t* vw = reinterpret_cast<uint32_t*>(page + page_v_codes_off(D));
-  for (int idx = lane; idx < 4 * 8 * ng; idx += 32) {
-    const int t = idx / (8 * ng), g = (idx / ng) % 8, w = idx % ng;
-    uint32_t word = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int ch = g + 8 * (4 * w + i);
-      word |= (uint32_t)vc[(2 * t) * D + ch] << (4 * i);
-      word |= (uint32_t)vc[(2 * t + 1) * D + ch] << (4 * (i + 4));
-    }
-    vw[idx] = word;
-  }
-  __syncwarp();
-}
-
-// shared scratch per warp for quantize_page_warp
-__host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D * 4 + 2 * 8 * D; }
-
-constexpr int kDemoteWarps = 4;
-
-template <typename T, int D>
-__global__ void __launch_bounds__(32 * kDemoteWarps) evict_demote_kernel(EvictParams p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int b = blockIdx.z, h = blockIdx.y;
-  const int warp = threadIdx.x >> 5;
-  const int n_tw_old = p.n_tier_old_tok / p.ws;
-  const int task = blockIdx.x * kDemoteWarps + warp;  // (candidate window, page i)
-  if (task >= (p.E - n_tw_old) * p.ppw) return;
-  const int cand = task / p.ppw, pi = task % p.ppw;
-  const int j = p.entrant[(int64_t)b * p.W + cand];
-  if (j < 0) return;  // candidate window dropped
-  const int w = n_tw_old + cand;
-  const int pos0 = p.s + w * p.ws + pi * kPageTokens;
-  const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
-  const int slot0 = go.fp_slot(pos0);
-  const int64_t rb = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + slot0) * p.D;
-  const T* ks = (const T*)p.k_src + rb;
-  const T* vs = (const T*)p.v_src + rb;
-  const int phys = p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + pi];
-  uint8_t* page = p.pages + (((int64_t)b * p.Hkv + h) * p.page_cap + phys) * page_bytes(D);
-  quantize_page_warp<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
-                        [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos,
-                        p.sin, page, smem_raw + warp * quant_scratch_bytes(D));
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(32 * kDemoteWarps) pack_pages_kernel(const T* k, const T* v,
-                                                                       int first_pos, int n_pages,
-                                                                       const float* cos, const float* sin,
-                                                                       uint8_t* out) {
+__global__ void __launch_bounds__(kApplyThreads, 3) evict_apply_kernel(EvictParams p, ApplyGrid a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int warp = threadIdx.x >> 5;
-  const int pg = blockIdx.x * kDemoteWarps + warp;
-  if (pg >= n_pages) return;
+  int bid = blockIdx.x;
+  if constexpr (D % kQGroup == 0) {  // the int4 tier needs whole 32-channel groups
+    if (bid < a.n_demote) {
+      demote_block<T, D>(p, a, bid, smem_raw);
+      return;
+    }
+  }
+  bid -= a.n_demote;
+  if (bid < a.n_gather) {
+    gather_block(p, a, bid);
+    return;
+  }
+  move_block<T, D>(p, a, bid - a.n_gather);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kApplyThreads) pack_pages_kernel(const T* k, const T* v, int first_pos,
+                                                                   const float* cos, const float* sin,
+                                                                   uint8_t* out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int pg = blockIdx.x;
   const T* ks = k + (int64_t)pg * 8 * D;
   const T* vs = v + (int64_t)pg * 8 * D;
-  quantize_page_warp<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
-                        [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); },
-                        first_pos + pg * 8, cos, sin, out + (int64_t)pg * page_bytes(D),
-                        smem_raw + warp * quant_scratch_bytes(D));
+  quantize_page_block<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
+                         [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, first_pos + pg * 8,
+                         cos, sin, out + (int64_t)pg * page_bytes(D), smem_raw);
 }
 
 size_t select_smem_bytes(int E, int R, int page_cap) {
-  return (size_t)8 * (E > 0 ? E : 1) + 4 * (256 + 32) + 4 * (size_t)(R > 0 ? R : 1) +
+  return (size_t)4 * (E > 0 ? E : 1) + 4 * (256 + 32) + 4 * (size_t)(R > 0 ? R : 1) +
          5 * (size_t)page_cap + 16;
+}
+
+template <typename T, int D>
+int launch_apply(EvictParams& p, cudaStream_t stream) {
+  ApplyGrid a{};
+  const int n_cand = p.E - p.n_tier_old_tok / p.ws;
+  a.demote_tasks = (D % kQGroup == 0 && p.tier && p.kprime > 0 && n_cand > 0) ? n_cand * p.ppw : 0;
+  a.n_demote = a.demote_tasks * p.Hkv * p.B;
+  a.gather_chunks = ceil_div(p.R + min(p.scores_cap - p.R, kTailWindows), kApplyThreads);
+  a.n_gather = a.gather_chunks * p.B;
+  a.n_fp_tok = p.T_new - p.n_tier_new_tok;  // sinks + fp windows kept
+  constexpr int tpb = kApplyThreads / (D / 2 / (16 / (int)sizeof(T)));
+  a.move_chunks = a.n_fp_tok > 0 ? ceil_div(a.n_fp_tok, tpb) : 0;
+  a.n_move = a.move_chunks * p.B;
+  const int64_t blocks = (int64_t)a.n_demote + a.n_gather + a.n_move;
+  if (blocks == 0) return SKV_OK;
+  if (blocks > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
+  const size_t smem = a.n_demote ? quant_scratch_bytes(D) : 0;
+  evict_apply_kernel<T, D><<<(unsigned)blocks, kApplyThreads, smem, stream>>>(p, a);
+  SKV_CHECK_LAUNCH();
+  return SKV_OK;
 }
 
 template <typename T>
@@ -428,28 +506,13 @@ int launch_evict(EvictParams& p, cudaStream_t stream) {
   cudaFuncSetAttribute(evict_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   evict_select_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
   SKV_CHECK_LAUNCH();
-  evict_gather_kernel<<<dim3(p.Hq, p.B), 256, 0, stream>>>(p);
-  SKV_CHECK_LAUNCH();
-  const int n_fp_tok = p.T_new - p.n_tier_new_tok;  // sinks + fp windows kept
-  if (n_fp_tok > 0) {
-    const int64_t work = (int64_t)n_fp_tok * (p.D / 2) / (16 / (int)sizeof(T));
-    dim3 grid((unsigned)ceil_div64(work, 256), p.Hkv, p.B);
-    evict_move_kernel<T><<<grid, 256, 0, stream>>>(p, n_fp_tok);
-    SKV_CHECK_LAUNCH();
+  switch (p.D) {
+    case 16: return launch_apply<T, 16>(p, stream);
+    case 32: return launch_apply<T, 32>(p, stream);
+    case 64: return launch_apply<T, 64>(p, stream);
+    case 128: return launch_apply<T, 128>(p, stream);
   }
-  const int n_cand = p.E - p.n_tier_old_tok / p.ws;
-  if (p.tier && p.kprime > 0 && n_cand > 0) {
-    dim3 grid((unsigned)ceil_div(n_cand * p.ppw, kDemoteWarps), p.Hkv, p.B);
-    const size_t sm = kDemoteWarps * quant_scratch_bytes(p.D);
-    switch (p.D) {
-      case 32: evict_demote_kernel<T, 32><<<grid, 32 * kDemoteWarps, sm, stream>>>(p); break;
-      case 64: evict_demote_kernel<T, 64><<<grid, 32 * kDemoteWarps, sm, stream>>>(p); break;
-      case 128: evict_demote_kernel<T, 128><<<grid, 32 * kDemoteWarps, sm, stream>>>(p); break;
-      default: return SKV_ERR_UNSUPPORTED;
-    }
-    SKV_CHECK_LAUNCH();
-  }
-  return SKV_OK;
+  return SKV_ERR_UNSUPPORTED;
 }
 
 int evict_dispatch(EvictParams& p, cudaStream_t stream) {
@@ -464,12 +527,12 @@ int evict_dispatch(EvictParams& p, cudaStream_t stream) {
 template <typename T>
 int launch_pack(const void* k, const void* v, int D, int first_pos, int n_pages, const float* cos,
                 const float* sin, uint8_t* out, cudaStream_t stream) {
-  dim3 grid(ceil_div(n_pages, kDemoteWarps));
-  const size_t smem = kDemoteWarps * quant_scratch_bytes(D);
+  const dim3 grid(n_pages);
+  const size_t smem = quant_scratch_bytes(D);
   switch (D) {
-    case 32: pack_pages_kernel<T, 32><<<grid, 32 * kDemoteWarps, smem, stream>>>((const T*)k, (const T*)v, first_pos, n_pages, cos, sin, out); break;
-    case 64: pack_pages_kernel<T, 64><<<grid, 32 * kDemoteWarps, smem, stream>>>((const T*)k, (const T*)v, first_pos, n_pages, cos, sin, out); break;
-    case 128: pack_pages_kernel<T, 128><<<grid, 32 * kDemoteWarps, smem, stream>>>((const T*)k, (const T*)v, first_pos, n_pages, cos, sin, out); break;
+    case 32: pack_pages_kernel<T, 32><<<grid, kApplyThreads, smem, stream>>>((const T*)k, (const T*)v, first_pos, cos, sin, out); break;
+    case 64: pack_pages_kernel<T, 64><<<grid, kApplyThreads, smem, stream>>>((const T*)k, (const T*)v, first_pos, cos, sin, out); break;
+    case 128: pack_pages_kernel<T, 128><<<grid, kApplyThreads, smem, stream>>>((const T*)k, (const T*)v, first_pos, cos, sin, out); break;
     default: return SKV_ERR_UNSUPPORTED;
   }
   SKV_CHECK_LAUNCH();
