@@ -63,7 +63,7 @@ __device__ int block_excl_scan(int v, int* smem, int& total) {
   return warp_off + x - v;
 }
 
-constexpr int kSelectThreads = 512;
+constexpr int kSelectThreads = 1024;
 // score/id slots initialised past the retained windows at each eviction: a
 // decode step adds at most two windows before the next eviction.
 constexpr int kTailWindows = 8;
@@ -87,9 +87,19 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   uint32_t thr = 0;
   int krem = 0;  // keys equal to thr that are kept, lowest window index first
   if (partial) {
+    const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
     for (int w = tid; w < E; w += nt) {
+      // heads summed in order; loads issued 16 at a time
       float acc = 0.f;
-      for (int h = 0; h < p.Hq; ++h) acc = __fadd_rn(acc, p.scores_src[((int64_t)b * p.Hq + h) * p.scores_cap + w]);
+      int h = 0;
+      for (; h + 16 <= p.Hq; h += 16) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc = __fadd_rn(acc, v[i]);
+      }
+      for (; h < p.Hq; ++h) acc = __fadd_rn(acc, rowp[(int64_t)h * p.scores_cap + w]);
       keys[w] = orderable(__fdiv_rn(acc, (float)p.Hq));
     }
     if (tid == 0) s_krem = k;
