@@ -21,6 +21,11 @@ Fixtures:
   eager_decode_<dt>.npz transformers eager_attention_forward +
                        compute_window_scores for one decode query
   prefill_scores.npz   the flash hook's chunked causal scoring math
+  cfg1_e2e.npz         the 2-layer Llama of tests/_cfg1.py generating 50 greedy
+                       tokens through the reference's eager backend (tokens,
+                       top-64 logits per step, final per-layer window ids,
+                       window scores, the last step's not yet accumulated
+                       scores, and seq length)
 """
 
 from __future__ import annotations
@@ -235,6 +240,57 @@ def gen_prefill_scores(scorer):
                         scores=to_np(sc))
 
 
+def gen_cfg1_e2e(ref_eager):
+    """Reference eager backend on the cfg1 model.  transformers 5.5 needs a
+    harness shim that changes no reference arithmetic: the Cache mask-size API
+    (``layers``, ``is_compileable``, ``get_mask_sizes``) and an eager attention
+    wrapper that trims the mask to the compacted key length (the 4.47
+    behaviour)."""
+    import transformers.models.llama.modeling_llama as LM
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("skv_cfg1", os.path.join(os.path.dirname(HERE), "_cfg1.py"))
+    C1 = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(C1)
+
+    class Shim(ref_eager.WindowedCache):
+        layers = []
+        is_compileable = False
+
+        def get_mask_sizes(self, q_len, layer_idx=0):
+            q = int(q_len.shape[0]) if torch.is_tensor(q_len) else int(q_len)
+            return self.get_seq_length(layer_idx) + q, 0
+
+    eager = LM.eager_attention_forward
+
+    def eager_trimmed(module, q, k, v, mask, *a, **kw):
+        if mask is not None:
+            mask = mask[..., : k.shape[-2]]
+        return eager(module, q, k, v, mask, *a, **kw)
+
+    LM.eager_attention_forward = eager_trimmed
+    try:
+        model = C1.build_model()
+        wcfg = ref_eager.WindowedCacheConfig(window_size=C1.WINDOW, num_sink_tokens=C1.SINKS,
+                                             local_window_size=C1.LOCAL, cache_budget=C1.BUDGET)
+        cache = Shim(config=wcfg, prefill_len=C1.PROMPT_LEN, model_config=model.config,
+                     kv_dtype=torch.float32, rope_module=model.model.rotary_emb,
+                     num_layers=2, max_tokens=C1.STEPS)
+        handles = ref_eager.install_score_hooks(model, cache, wcfg)
+        toks, top_i, top_v = C1.greedy(model, cache, C1.prompt(), output_attentions=True)
+        handles.remove()
+    finally:
+        LM.eager_attention_forward = eager
+    rec = dict(tokens=np.array(toks, np.int64), top_i=top_i.astype(np.int64), top_v=top_v.astype(np.float32),
+               seq_len=np.array(cache.get_seq_length(0)))
+    for li in range(2):
+        st = cache._states[li]
+        rec[f"ids_{li}"] = to_np(st.original_window_ids)
+        rec[f"scores_{li}"] = to_np(st.window_scores)
+        # the last step's scores wait in cache_kwargs for the next update()
+        rec[f"pending_{li}"] = to_np(cache.cache_kwargs[li]["window_scores"])
+    np.savez_compressed(os.path.join(HERE, "cfg1_e2e.npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -253,6 +309,8 @@ def main():
     gen_cache_drive(WindowedCache, WindowedCacheConfig)
     gen_eager_decode(scorer)
     gen_prefill_scores(scorer)
+    import modules.windowed_eager_cache as ref_eager
+    gen_cfg1_e2e(ref_eager)
     print("golden fixtures written to", HERE)
 
 

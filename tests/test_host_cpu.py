@@ -231,3 +231,19 @@ def test_no_per_token_python_loops_in_host_hot_path():
         for node in ast.walk(ast.parse(inspect.getsource(mod))):
             if isinstance(node, ast.For) and isinstance(node.target, ast.Name):
                 assert node.target.id.lower() not in banned, (mod.__name__, node.target.id)
+
+
+def test_cfg1_model_and_prompt_reproduce_the_golden_prefill():
+    """The end-to-end fixture's model is rebuilt from seeds on every machine:
+    its plain-transformers prefill (no cache, full attention) must give the
+    first-step logits the reference recorded."""
+    import numpy as np
+    import torch
+
+    from tests import _cfg1 as C1
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "cfg1_e2e.npz"))
+    model = C1.build_model()
+    with torch.no_grad():
+        lg = model(input_ids=C1.prompt(), use_cache=False).logits[0, -1].float()
+    assert int(lg.argmax()) == int(z["tokens"][0])
+    np.testing.assert_allclose(lg[torch.as_tensor(z["top_i"][0])].numpy(), z["top_v"][0], atol=1e-5, rtol=0)
