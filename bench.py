@@ -314,44 +314,48 @@ def cpu_step(oc, rng):
     oc._pending = sc
 
 
-def cpu_baseline(seconds: float = 10.0, rows: int = 1):
-    import numpy as np
-    oc, rng = cpu_reference_setup(rows)
-    cpu_step(oc, rng)
-    n = 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < seconds or n < WS:
-        cpu_step(oc, rng)
-        n += 1
-    dt = time.perf_counter() - t0
+def _all_host_threads():
+    """BLAS thread pools sized to every host core (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks); returns (context, threads)."""
+    n = os.cpu_count() or 1
     try:
         import threadpoolctl
-        info = threadpoolctl.threadpool_info()
-        cores = max([i.get("num_threads", 1) for i in info] + [1])
+        return threadpoolctl.threadpool_limits(limits=n), n
     except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
+        import contextlib
+        return contextlib.nullcontext(), 1
+
+
+def cpu_baseline(seconds: float = 10.0, rows: int = 1):
+    ctx, cores = _all_host_threads()
+    with ctx:
+        oc, rng = cpu_reference_setup(rows)
+        cpu_step(oc, rng)
+        n = 0
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n < WS:
+            cpu_step(oc, rng)
+            n += 1
+        dt = time.perf_counter() - t0
     return {"value": rows * n / dt, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{rows} of {B} rows, {n} decode steps (incl. {n // WS} evictions), "
                       f"all-fp16 retained cache of {oc.seq_length} tokens (reference has no int4 tier); "
-                      f"numpy restatement of the reference eager path, host cores = {os.cpu_count()}"}
+                      f"numpy restatement of the reference eager path (BLAS on {cores} threads)"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    oc, rng = cpu_reference_setup(1)
-    for _ in range(args.warmup):
-        cpu_step(oc, rng)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_step(oc, rng)
-    dt = time.perf_counter() - t0
+    ctx, cores = _all_host_threads()
+    with ctx:
+        oc, rng = cpu_reference_setup(1)
+        for _ in range(args.warmup):
+            cpu_step(oc, rng)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cpu_step(oc, rng)
+        dt = time.perf_counter() - t0
     value = 1 * args.steps / dt
-    try:
-        import threadpoolctl
-        cores = max([i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()] + [1])
-    except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,

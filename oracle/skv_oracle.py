@@ -415,16 +415,19 @@ def eager_decode_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scaling:
     weights cast to the model dtype).  q [B,Hq,D]; k,v [B,Hkv,S,D].
     Returns (out [B,Hq,D] fp32, window_scores [B,Hq,W] fp32)."""
     B, Hq, D = q.shape
-    Hkv = k.shape[1]
+    Hkv, S = k.shape[1], k.shape[2]
     G = Hq // Hkv
-    kx = np.repeat(k, G, axis=1).astype(np.float32)
-    vx = np.repeat(v, G, axis=1).astype(np.float32)
-    logits = np.einsum("bhd,bhsd->bhs", q.astype(np.float32), kx).astype(np.float32) * np.float32(scaling)
+    # query head h reads kv head h // G (repeat_kv); grouped instead of
+    # materialised: [B, Hkv, G, D] @ [B, Hkv, D, S]
+    qg = q.astype(np.float32, copy=False).reshape(B, Hkv, G, D)
+    kf = k.astype(np.float32, copy=False)
+    vf = v.astype(np.float32, copy=False)
+    logits = np.matmul(qg, kf.transpose(0, 1, 3, 2)).reshape(B, Hq, S) * np.float32(scaling)
     m = logits.max(axis=-1, keepdims=True)
     e = np.exp((logits - m).astype(np.float32))
     p = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
     p_d = round_to(p, dtype)
-    out = np.einsum("bhs,bhsd->bhd", p_d, vx).astype(np.float32)
+    out = np.matmul(p_d.reshape(B, Hkv, G, S), vf).reshape(B, Hq, D).astype(np.float32, copy=False)
     scores = reduce_token_scores_to_windows(p_d, num_sink, window_size)
     return out, scores
 
