@@ -235,8 +235,9 @@ def run_ours(args, rank, world, dev):
         return None
     peak, peak_kind = measured_hbm_peak()
     achieved = bytes_per_launch / (attn_avg * 1e-3) / 1e9
-    launches_per_step = 1 + 2  # append + decode (+ merge)
-    gpu_launches = args.steps * launches_per_step + n_evict * 3
+    # every step: decode with its fused append, then the split merge; an
+    # evicting step appends on its own and adds the select and apply kernels
+    gpu_launches = args.steps * 2 + n_evict * 3
     traffic = None
     tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tp):

@@ -17,6 +17,8 @@
  *                            modules/windowed_cache/scorer.py:17-109,
  *                            WindowedCache.update score accumulation
  *                            modules/windowed_cache/cache.py:163-228
+ *   skv_decode_attention_append  skv_append + skv_decode_attention of one
+ *                            decode step (state.py:68-119 + the above)
  *   skv_evict                WindowedCache.update eviction block
  *                            modules/windowed_cache/cache.py:230-286 =
  *                            EvictionPolicy.compute_retain_window_indices +
@@ -159,6 +161,25 @@ int skv_decode_attention(const skv_layer_desc* layer, int32_t seq_len, int32_t t
                          int64_t out_stride_b, int64_t out_stride_h, float scaling,
                          float* window_scores, int32_t scores_capacity, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/*
+ * One decode step with its token append fused in: the effect of
+ *   skv_append(layer, seq_len - 1, tier_pages, k_new, v_new, stride_b,
+ *              stride_h, 0, 1, stream)
+ * followed by skv_decode_attention(layer, seq_len, ...), in one launch on the
+ * tensor-core path (the block that reads the last unit writes the new key and
+ * value first).  seq_len counts the new token; k_new/v_new hold one token per
+ * (row, kv head) with element strides (stride_b, stride_h).  Replaces the
+ * reference's update() append (modules/windowed_cache/state.py:68-119, a
+ * torch.cat) and the attention that follows it in the same layer call.
+ */
+int skv_decode_attention_append(const skv_layer_desc* layer, int32_t seq_len, int32_t tier_pages,
+                                const void* k_new, const void* v_new, int64_t stride_b,
+                                int64_t stride_h, const void* q, int64_t q_stride_b,
+                                int64_t q_stride_h, void* out, int64_t out_stride_b,
+                                int64_t out_stride_h, float scaling, float* window_scores,
+                                int32_t scores_capacity, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /*
  * skv_decode_attention without a workspace argument (no counterpart in the

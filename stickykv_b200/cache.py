@@ -50,7 +50,7 @@ def _stream(device: torch.device) -> int:
 class _Side:
     """One half of the ping-pong state."""
 
-    __slots__ = ("k", "v", "table", "scores", "ids")
+    __slots__ = ("k", "v", "table", "scores", "ids", "desc", "desc_key")
 
     def __init__(self) -> None:
         self.k: Optional[Tensor] = None
@@ -58,6 +58,8 @@ class _Side:
         self.table: Optional[Tensor] = None
         self.scores: Optional[Tensor] = None
         self.ids: Optional[Tensor] = None
+        self.desc: Optional[LayerDesc] = None   # ABI descriptor of this side, rebuilt when
+        self.desc_key: Optional[tuple] = None   # its buffers or the rope table change
 
 
 class LayerState:
@@ -78,6 +80,10 @@ class LayerState:
         self.next_window_id = 0
         self.last_update_prefill = False
         self.allocated = False
+        # one decode token whose append is fused into the next decode call
+        self.pending: Optional[Tuple[Tensor, Tensor]] = None
+        self.flush = None  # writes a pending token (set by the cache)
+        self.decode_ws, self.decode_ws_T = 0, 0  # decode workspace bytes, valid up to decode_ws_T
         # geometry copied at allocation
         self.B = self.Hkv = self.Hq = self.D = 0
         self.dtype: Optional[torch.dtype] = None
@@ -90,6 +96,8 @@ class LayerState:
     def _fp_view(self, which: str) -> Optional[Tensor]:
         if not self.allocated:
             return None
+        if self.pending is not None:
+            self.flush(self)
         if self.tier_pages:
             raise NotImplementedError(
                 "key_states/value_states of an int4-tier cache are not materialised; "
@@ -163,7 +171,7 @@ class WindowedCache(_HFCacheBase):
         self.telemetry = telemetry if telemetry is not None else NullTelemetry()
         self.tier = bool(config.int4_tier)
         self.local_windows = self.resolved.local_tokens // self.resolved.window_size
-        self._states: List[LayerState] = [LayerState() for _ in range(num_layers)]
+        self._states: List[LayerState] = [self._new_state() for _ in range(num_layers)]
         self._generation_step: List[int] = [0] * num_layers
         self._prefill_done: List[bool] = [False] * num_layers
         self.cache_kwargs: Dict[int, Dict[str, Any]] = {i: {} for i in range(num_layers)}
@@ -223,10 +231,15 @@ class WindowedCache(_HFCacheBase):
 
     def reset(self) -> None:
         for i in range(self.num_layers):
-            self._states[i] = LayerState()
+            self._states[i] = self._new_state()
             self._generation_step[i] = 0
             self._prefill_done[i] = False
             self.cache_kwargs[i] = {}
+
+    def _new_state(self) -> LayerState:
+        st = LayerState()
+        st.flush = self._flush
+        return st
 
     # -- allocation ------------------------------------------------------------------------
     def _caps(self, P: int) -> Tuple[int, int, int, int]:
@@ -298,6 +311,10 @@ class WindowedCache(_HFCacheBase):
             setattr(side, name, new)
 
     def _desc(self, st: LayerState, side: _Side) -> LayerDesc:
+        key = (side.k.data_ptr(), side.v.data_ptr(), side.k.shape[2],
+               None if side.table is None else side.table.data_ptr(), self._rope_positions)
+        if side.desc_key == key:
+            return side.desc
         r = self.resolved
         d = LayerDesc()
         d.batch, d.num_kv_heads, d.num_q_heads, d.head_dim = st.B, st.Hkv, st.Hq, st.D
@@ -312,6 +329,7 @@ class WindowedCache(_HFCacheBase):
             d.tier_table = side.table.data_ptr()
         d.rope_cos, d.rope_sin = self._rope[0].data_ptr(), self._rope[1].data_ptr()
         d.rope_positions = self._rope_positions
+        side.desc, side.desc_key = d, key
         return d
 
     def _fp_slots(self, T: int, tier_pages: int) -> int:
@@ -328,42 +346,71 @@ class WindowedCache(_HFCacheBase):
     # -- update (reference cache.py:110-293) ------------------------------------------------
     def update(self, key_states: Tensor, value_states: Tensor, layer_idx: int,
                cache_kwargs: Optional[Dict[str, Any]] = None) -> Tuple[Tensor, Tensor]:
+        """Append this step's keys/values, accumulate external window scores,
+        evict every ``window_size`` decode steps.  Returns the step's own
+        key/value states: the ``stickykv_b200`` attention reads the cache
+        directly.  A one-token decode step that does not evict defers its
+        append to the attention call, which fuses it into the same launch
+        (``skv_decode_attention_append``); the length already counts it."""
         st = self._states[layer_idx]
         n_new = key_states.shape[2]
         if not st.allocated:
             self._allocate(st, key_states, max(n_new, self.prefill_len))
-        self._append(st, key_states, value_states)
+        if st.pending is not None:
+            self._flush(st)
         is_prefill = not self._prefill_done[layer_idx]
         self._prefill_done[layer_idx] = True
         st.last_update_prefill = is_prefill
 
-        merged: Dict[str, Any] = dict(cache_kwargs or {})
-        merged.update(self.cache_kwargs.get(layer_idx, {}))
-        ext = merged.get("window_scores")
         lk = self.cache_kwargs.get(layer_idx)
-        if lk is not None and "window_scores" in lk:
-            del lk["window_scores"]
-        if ext is not None:
-            self._add_scores(st, ext)
+        if cache_kwargs or lk:
+            merged: Dict[str, Any] = dict(cache_kwargs or {})
+            merged.update(lk or {})
+            ext = merged.get("window_scores")
+            if lk is not None and "window_scores" in lk:
+                del lk["window_scores"]
+            if ext is not None:
+                self._add_scores(st, ext)
 
         step = self._generation_step[layer_idx]
         ws = self.resolved.window_size
-        if not is_prefill and step > 0 and step % ws == 0 and st.has_scores:
+        evict = not is_prefill and step > 0 and step % ws == 0 and st.has_scores
+        if not is_prefill and n_new == 1 and not evict:
+            self._defer_append(st, key_states, value_states)
+        else:
+            self._append(st, key_states, value_states)
+        if evict:
             self._evict(st, layer_idx, step)
         if not is_prefill:
             self._generation_step[layer_idx] = step + 1
-        if is_prefill:
-            return key_states, value_states
-        side = st.sides[st.cur]
-        n = self._fp_slots(st.T, st.tier_pages)
-        return side.k[:, :, :n], side.v[:, :, :n]
+        return key_states, value_states
+
+    @staticmethod
+    def _kv_ok(k: Tensor, v: Tensor) -> bool:
+        es = k.element_size()
+        return (k.stride() == v.stride() and k.stride(-1) == 1 and k.data_ptr() % 16 == 0
+                and v.data_ptr() % 16 == 0 and all((x * es) % 16 == 0 for x in k.stride()[:3]))
+
+    def _defer_append(self, st: LayerState, k: Tensor, v: Tensor) -> None:
+        if not self._kv_ok(k, v):
+            k, v = k.contiguous(), v.contiguous()
+        self._grow_side(st, st.sides[st.cur], self._fp_slots(st.T + 1, st.tier_pages))
+        self._ensure_rope(st.T + 67, st.D, st.device)
+        st.pending = (k, v)
+        st.T += 1
+
+    def _flush(self, st: LayerState) -> None:
+        """Write a deferred decode token with a plain append."""
+        k, v = st.pending
+        st.pending = None
+        d = self._desc(st, st.sides[st.cur])
+        check(lib().skv_append(C.byref(d), st.T - 1, st.tier_pages, k.data_ptr(), v.data_ptr(),
+                               k.stride(0), k.stride(1), k.stride(2), 1, _stream(st.device)),
+              "skv_append")
 
     def _append(self, st: LayerState, k: Tensor, v: Tensor) -> None:
         n_new = k.shape[2]
-        es = k.element_size()
-        ok = (k.stride() == v.stride() and k.stride(-1) == 1 and k.data_ptr() % 16 == 0
-              and v.data_ptr() % 16 == 0 and all((x * es) % 16 == 0 for x in k.stride()[:3]))
-        if not ok:
+        if not self._kv_ok(k, v):
             k, v = k.contiguous(), v.contiguous()
         side = st.sides[st.cur]
         need = self._fp_slots(st.T + n_new, st.tier_pages)
@@ -457,23 +504,34 @@ class WindowedCache(_HFCacheBase):
     # -- attention entry points (called by the stickykv_b200 attention function) ----------
     def decode_attention(self, layer_idx: int, query: Tensor, scaling: float) -> Tensor:
         """One-token attention over the retained cache; accumulates window mass.
-        query [B, Hq, 1, D] -> out [B, 1, Hq, D]."""
+        query [B, Hq, 1, D] -> out [B, 1, Hq, D].  A deferred append of this
+        step's token runs in the same native call."""
         st = self._states[layer_idx]
-        q = query[:, :, 0, :]
-        if q.stride(-1) != 1:
-            q = q.contiguous()
+        if query.stride(-1) != 1:
+            query = query.contiguous()
         out = torch.empty(st.B, 1, st.Hq, st.D, dtype=st.dtype, device=st.device)
-        o = out[:, 0]
         side = st.sides[st.cur]
         d = self._desc(st, side)
         L = lib()
-        nbytes = L.skv_decode_workspace_size(C.byref(d), st.T)
-        ws = self._workspace(nbytes, st.device)
-        check(L.skv_decode_attention(C.byref(d), st.T, st.tier_pages, q.data_ptr(), q.stride(0),
-                                     q.stride(1), o.data_ptr(), o.stride(0), o.stride(1),
-                                     float(scaling), side.scores.data_ptr(), st.scores_cap,
-                                     ws.data_ptr(), ws.numel(), _stream(st.device)),
-              "skv_decode_attention")
+        if st.T > st.decode_ws_T:  # workspace sized for twice the length, re-queried rarely
+            st.decode_ws_T = 2 * st.T
+            st.decode_ws = L.skv_decode_workspace_size(C.byref(d), st.decode_ws_T)
+        ws = self._workspace(st.decode_ws, st.device)
+        # q[:, :, 0, :] and out[:, 0] by strides (no views)
+        qs_b, qs_h, os_b, os_h = query.stride(0), query.stride(1), out.stride(0), out.stride(2)
+        if st.pending is not None:
+            k, v = st.pending
+            st.pending = None
+            check(L.skv_decode_attention_append(
+                C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                query.data_ptr(), qs_b, qs_h, out.data_ptr(), os_b, os_h, float(scaling),
+                side.scores.data_ptr(), st.scores_cap, ws.data_ptr(), ws.numel(), _stream(st.device)),
+                "skv_decode_attention_append")
+        else:
+            check(L.skv_decode_attention(
+                C.byref(d), st.T, st.tier_pages, query.data_ptr(), qs_b, qs_h, out.data_ptr(), os_b,
+                os_h, float(scaling), side.scores.data_ptr(), st.scores_cap, ws.data_ptr(), ws.numel(),
+                _stream(st.device)), "skv_decode_attention")
         self._note_windows(st)
         return out
 

@@ -24,7 +24,8 @@ bool decode_mma_length_ok(int T);
 size_t decode_mma_ws_size(const skv_layer_desc* L, int T);
 int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, int64_t q_sb,
                int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float scaling, float* scores,
-               int scores_cap, void* ws, cudaStream_t stream);
+               int scores_cap, void* ws, cudaStream_t stream, const void* k_new = nullptr,
+               const void* v_new = nullptr, int64_t kn_sb = 0, int64_t kn_sh = 0);
 int evict_dispatch(EvictParams& p, cudaStream_t stream);
 int pack_pages_dispatch(const skv_layer_desc* L, const void* k, const void* v, int first_pos,
                         int n_pages, uint8_t* out, cudaStream_t stream);
@@ -167,10 +168,8 @@ size_t skv_decode_workspace_size(const skv_layer_desc* L, int32_t T) {
   return a;
 }
 
-int skv_decode_attention(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q,
-                         int64_t q_sb, int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh,
-                         float scaling, float* scores, int32_t scores_cap, void* ws, size_t ws_bytes,
-                         void* stream) {
+static int check_decode(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,
+                        float* scores, int32_t scores_cap, void* ws, size_t ws_bytes) {
   int rc = check_layer(L);
   if (rc) return rc;
   if (T <= 0 || !q || !out) return SKV_ERR_INVALID_ARG;
@@ -180,9 +179,38 @@ int skv_decode_attention(const skv_layer_desc* L, int32_t T, int32_t tier_pages,
   if (tier_pages > 0 && L->rope_positions < L->num_sink + tier_pages * kPageTokens) return SKV_ERR_CAPACITY;
   if (!ws || ws_bytes < skv_decode_workspace_size(L, T)) return SKV_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return SKV_ERR_MISALIGNED;
+  return SKV_OK;
+}
+
+int skv_decode_attention(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q,
+                         int64_t q_sb, int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh,
+                         float scaling, float* scores, int32_t scores_cap, void* ws, size_t ws_bytes,
+                         void* stream) {
+  const int rc = check_decode(L, T, tier_pages, q, out, scores, scores_cap, ws, ws_bytes);
+  if (rc) return rc;
   const cudaStream_t s = (cudaStream_t)stream;
   if (decode_mma_supported(L) && decode_mma_length_ok(T))
     return decode_mma(L, T, tier_pages, q, q_sb, q_sh, out, o_sb, o_sh, scaling, scores, scores_cap, ws, s);
+  return decode_generic(L, T, tier_pages, q, q_sb, q_sh, out, o_sb, o_sh, scaling, scores, scores_cap, ws, s);
+}
+
+int skv_decode_attention_append(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* k_new,
+                                const void* v_new, int64_t sb, int64_t sh, const void* q, int64_t q_sb,
+                                int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float scaling,
+                                float* scores, int32_t scores_cap, void* ws, size_t ws_bytes, void* stream) {
+  // every check of both halves runs before anything is launched
+  int rc = check_decode(L, T, tier_pages, q, out, scores, scores_cap, ws, ws_bytes);
+  if (rc) return rc;
+  if (!k_new || !v_new || T - 1 < 0) return SKV_ERR_INVALID_ARG;
+  if (tier_pages > 0 && T - 1 < L->num_sink + tier_pages * kPageTokens) return SKV_ERR_INVALID_ARG;
+  const int es = elt_size(L->kv_dtype);
+  if (!aligned(k_new, 16) || !aligned(v_new, 16)) return SKV_ERR_MISALIGNED;
+  if ((sb * es) % 16 || (sh * es) % 16 || (L->head_dim * es) % 16) return SKV_ERR_MISALIGNED;
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (decode_mma_supported(L) && decode_mma_length_ok(T))
+    return decode_mma(L, T, tier_pages, q, q_sb, q_sh, out, o_sb, o_sh, scaling, scores, scores_cap, ws, s,
+                      k_new, v_new, sb, sh);
+  if ((rc = append_dispatch(L, T - 1, tier_pages, k_new, v_new, sb, sh, 0, 1, s))) return rc;
   return decode_generic(L, T, tier_pages, q, q_sb, q_sh, out, o_sb, o_sh, scaling, scores, scores_cap, ws, s);
 }
 

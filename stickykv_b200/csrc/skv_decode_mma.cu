@@ -83,7 +83,10 @@ struct MmaParams {
   float* scores;   // [B][Hq][scores_cap] accumulator (may be null)
   float* part;     // [B][Hkv][n_split][4][D+2]: O, max (log2 domain), sum
   float* mass;     // [B][Hq][W]: window mass relative to its split's max
-  int64_t q_sb, q_sh, o_sb, o_sh;
+  const void* k_new;  // optional token appended by the last split's blocks
+  const void* v_new;
+  int64_t q_sb, q_sh, o_sb, o_sh, kn_sb, kn_sh;
+  int new_slot;       // fp slot of the appended token
   int B, Hkv, cap, page_cap, scores_cap, n_split;
   int s, s_eff, s_pad, NS, n_tp, rest, U, W, rope_rows;
   float scale_log2;
@@ -276,6 +279,19 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   float* mass_s = reinterpret_cast<float*>(smem + C::kRingBytes);  // [tile][12]
   int* tbl = reinterpret_cast<int*>(smem + C::kRingBytes + C::kMassBytes);  // [unit - u0]
 
+  if (p.k_new != nullptr && split == p.n_split - 1) {
+    // fused append: the last unit holds the new token; write its key and
+    // value rows before any copy of this block reads them (the barrier below
+    // orders the stores before the cp.async reads)
+    constexpr int VPR = D / 8;  // 16-byte vectors per row
+    const int64_t row = (((int64_t)b * p.Hkv + kh) * p.cap + p.new_slot) * D;
+    for (int e = threadIdx.x; e < 2 * VPR; e += kThreads) {
+      const int which = e / VPR, c = e - which * VPR;
+      const T* src = (const T*)(which ? p.v_new : p.k_new) + b * p.kn_sb + kh * p.kn_sh + c * 8;
+      T* dst = (T*)(which ? p.v_fp : p.k_fp) + row + c * 8;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+  }
   {  // page table slice, indexed by unit offset within the split
     const int k0 = max(0, R.NS - u0), k1 = min(u1, R.TB) - u0;
     const int32_t* src = p.table + (int64_t)b * p.page_cap + (u0 - R.NS);
@@ -982,9 +998,16 @@ size_t decode_mma_ws_size(const skv_layer_desc* L, int T) { return mma_ws(L, T).
 
 int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, int64_t q_sb, int64_t q_sh,
                void* out, int64_t o_sb, int64_t o_sh, float scaling, float* scores, int scores_cap, void* ws,
-               cudaStream_t stream) {
+               cudaStream_t stream, const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh) {
   if ((q_sb % 2) || (q_sh % 2) || ((uintptr_t)q % 4)) return SKV_ERR_MISALIGNED;  // 32-bit query loads
   MmaParams p{};
+  if (k_new != nullptr) {
+    p.k_new = k_new;
+    p.v_new = v_new;
+    p.kn_sb = kn_sb;
+    p.kn_sh = kn_sh;
+    p.new_slot = Geometry{L->num_sink, L->sink_pad, L->window_size, T, tier_pages * kPageTokens}.fp_slot(T - 1);
+  }
   const MmaWs w = mma_ws(L, T);
   p.k_fp = L->k_fp; p.v_fp = L->v_fp; p.pages = L->tier_pages; p.table = L->tier_table;
   p.cos = L->rope_cos; p.sin = L->rope_sin; p.q = q; p.out = out; p.scores = scores;

@@ -335,3 +335,64 @@ def test_cfg3_scale_eviction_selection_and_codes():
             kc, ks, kz = O.quantize_group32(kf)
             np.testing.assert_array_equal(codes[0][b, :, j * 8:(j + 1) * 8], kc)
             np.testing.assert_array_equal(codes[1][b, :, j * 8:(j + 1) * 8], ks)
+
+
+@pytest.mark.parametrize("dt,D,G,tier", [("f16", 64, 4, True), ("bf16", 128, 4, False),
+                                         ("bf16", 64, 4, True), ("f32", 64, 2, False)])
+def test_fused_append_decode_matches_append_then_decode(dt, D, G, tier):
+    """skv_decode_attention_append == skv_append + skv_decode_attention, bit
+    for bit: output, window scores and the fp store (tensor-core path for the
+    fp16/bf16 GQA-4 cases, the portable path for fp32 GQA-2)."""
+    import ctypes as Ct
+    from stickykv_b200 import _lib
+    L = _lib.lib()
+    g = torch.Generator().manual_seed(D + G)
+    B, Hkv, P = 2, 2, 611
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, P + 64)
+    cache = make_cache(dt, B, Hkv, Hq, D, P, 16, cos, sin, tier=tier)
+    cache.update(rand((B, Hkv, P, D), dt, g).to(DEV), rand((B, Hkv, P, D), dt, g).to(DEV), 0)
+    st = cache._states[0]
+    W = math.ceil((P - 4) / 8)
+    st.sides[st.cur].scores[:, :, :W] = torch.rand(B, Hq, W, generator=g).to(DEV)
+    st.has_scores, st.W, st.next_window_id = True, W, W
+    for _ in range(9):  # one eviction
+        k1 = rand((B, Hkv, 1, D), dt, g).to(DEV)
+        cache.update(k1, k1.clone(), 0)
+    if st.pending is not None:
+        cache._flush(st)
+    assert (st.tier_pages > 0) == tier
+    side = st.sides[st.cur]
+    d = cache._desc(st, side)
+    T0 = st.T
+    stream = torch.cuda.current_stream().cuda_stream
+    kn = rand((B, Hkv, 1, D), dt, g).to(DEV)
+    vn = rand((B, Hkv, 1, D), dt, g).to(DEV)
+    q = rand((B, Hq, D), dt, g, scale=2.0).to(DEV)
+    nbytes = L.skv_decode_workspace_size(Ct.byref(d), T0 + 1)
+    runs = []
+    for fused in (False, True):
+        k, v, sc = side.k.clone(), side.v.clone(), side.scores.clone()
+        dd = _lib.LayerDesc.from_buffer_copy(d)
+        dd.k_fp, dd.v_fp = k.data_ptr(), v.data_ptr()
+        out = torch.empty(B, Hq, D, dtype=q.dtype, device=DEV)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+        if fused:
+            rc = L.skv_decode_attention_append(Ct.byref(dd), T0 + 1, st.tier_pages, kn.data_ptr(), vn.data_ptr(),
+                                               kn.stride(0), kn.stride(1), q.data_ptr(), q.stride(0), q.stride(1),
+                                               out.data_ptr(), out.stride(0), out.stride(1), Ct.c_float(D ** -0.5),
+                                               sc.data_ptr(), st.scores_cap, ws.data_ptr(), nbytes, stream)
+            assert rc == 0, L.skv_last_cuda_error()
+        else:
+            assert L.skv_append(Ct.byref(dd), T0, st.tier_pages, kn.data_ptr(), vn.data_ptr(), kn.stride(0),
+                                kn.stride(1), kn.stride(2), 1, stream) == 0
+            rc = L.skv_decode_attention(Ct.byref(dd), T0 + 1, st.tier_pages, q.data_ptr(), q.stride(0),
+                                        q.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+                                        Ct.c_float(D ** -0.5), sc.data_ptr(), st.scores_cap, ws.data_ptr(),
+                                        nbytes, stream)
+            assert rc == 0, L.skv_last_cuda_error()
+        torch.cuda.synchronize()
+        runs.append((out, sc, k, v))
+    for name, a, b in zip(("out", "scores", "k", "v"), *runs):
+        bad = (a != b) & ~(torch.isnan(a) & torch.isnan(b))
+        assert not bad.any(), f"{name}: {int(bad.sum())} differ, first at {bad.nonzero()[0].tolist()} (T0={T0})"

@@ -84,6 +84,18 @@ def test_null_arguments_are_rejected_without_a_gpu():
     d.num_q_heads, d.sink_pad, d.num_sink = 4, 0, 3                                # sink_pad != 8
     assert L.skv_decode_attention(ctypes.byref(d), 8, 0, 16, 0, 0, 16, 0, 0, 1.0, None, 0, None, 0,
                                   None) == 1
+    # the fused append + decode runs every check of both halves before any launch
+    assert L.skv_decode_attention_append(None, 1, 0, 16, 16, 0, 0, 16, 0, 0, 16, 0, 0, 1.0, None, 0,
+                                         None, 0, None) == 1
+    d.sink_pad = 8
+    assert L.skv_decode_attention_append(ctypes.byref(d), 8, 0, 16, 16, 0, 0, 16, 0, 0, 16, 0, 0, 1.0,
+                                         None, 0, None, 0, None) == 6              # no workspace
+    assert L.skv_decode_attention_append(ctypes.byref(d), 80, 0, 16, 16, 0, 0, 16, 0, 0, 16, 0, 0, 1.0,
+                                         None, 0, 256, 1 << 20, None) == 4         # past capacity
+    assert L.skv_decode_attention_append(ctypes.byref(d), 8, 0, None, 16, 0, 0, 16, 0, 0, 16, 0, 0,
+                                         1.0, None, 0, 256, 1 << 20, None) == 1    # null k_new
+    assert L.skv_decode_attention_append(ctypes.byref(d), 8, 0, 24, 16, 0, 0, 16, 0, 0, 16, 0, 0, 1.0,
+                                         None, 0, 256, 1 << 20, None) == 3         # misaligned k_new
 
 
 @pytest.mark.parametrize("seed", range(6))
