@@ -139,6 +139,19 @@ struct Geometry {
   __host__ __device__ int fp_slot(int pos) const { return pos < s ? pos : s_pad + (pos - s - n_tier); }
 };
 
+// parameters of the prefill kernels (skv_prefill.cu, skv_prefill_mma.cu)
+struct PrefillParams {
+  const void* q;  // [B][Hq][T][D]
+  const void* k;  // [B][Hkv][T][D]
+  const void* v;
+  void* out;      // [B][T][Hq][D]
+  float* lse;     // [B][Hq][T]
+  float* colmass; // [B][Hq][T]
+  float* scores;  // [B][Hq][cap] (+=)
+  int B, Hq, Hkv, T, D, cap, s, ws;
+  float scaling;
+};
+
 // parameters of the eviction kernels (skv_evict.cu), filled by skv_capi.cu
 struct EvictParams {
   // geometry

@@ -6,7 +6,8 @@
 // same pass, produces the prompt's attention output, so the prompt's K is not
 // re-read by a second attention kernel.
 //
-// Portable CUDA-core version: pass 1 computes each row's output and
+// Portable CUDA-core version (fp32, and head dims without a tensor-core
+// kernel; fp16/bf16 at head_dim 64/128 run skv_prefill_mma.cu): pass 1 computes each row's output and
 // log-sum-exp with an online softmax (one warp per query row); pass 2 sums
 // exp(s_ij - lse_i) over rows i >= j for each key column j (one warp per
 // column); pass 3 reduces the column mass to windows in a fixed order.
@@ -15,18 +16,6 @@
 #include "skv_common.cuh"
 
 namespace skv {
-
-struct PrefillParams {
-  const void* q;  // [B][Hq][T][D]
-  const void* k;  // [B][Hkv][T][D]
-  const void* v;
-  void* out;      // [B][T][Hq][D]
-  float* lse;     // [B][Hq][T]
-  float* colmass; // [B][Hq][T]
-  float* scores;  // [B][Hq][cap] (+=)
-  int B, Hq, Hkv, T, D, cap, s, ws;
-  float scaling;
-};
 
 constexpr int kMaxDPerLane = 4;  // head_dim <= 128
 
@@ -137,6 +126,9 @@ int launch_prefill(PrefillParams& p, cudaStream_t stream) {
   return SKV_OK;
 }
 
+bool prefill_mma_supported(const skv_layer_desc* L);
+int prefill_mma(const PrefillParams& p, int dtype, bool colmass, cudaStream_t stream);
+
 int prefill_dispatch(const skv_layer_desc* L, int T, const void* q, const void* k, const void* v,
                      void* out, float scaling, float* scores, int scores_cap, void* ws,
                      cudaStream_t stream) {
@@ -148,6 +140,14 @@ int prefill_dispatch(const skv_layer_desc* L, int T, const void* q, const void* 
   p.scores = scores;
   p.B = L->batch; p.Hq = L->num_q_heads; p.Hkv = L->num_kv_heads; p.T = T; p.D = L->head_dim;
   p.cap = scores_cap; p.s = L->num_sink; p.ws = L->window_size; p.scaling = scaling;
+  if (prefill_mma_supported(L)) {  // tensor cores: output + lse, column mass, then windows
+    int rc = prefill_mma(p, L->kv_dtype, scores != nullptr, stream);
+    if (rc || !scores) return rc;
+    dim3 g2(ceil_div(ceil_div(p.T, p.ws), 128), p.Hq, p.B);
+    prefill_windows_kernel<<<g2, 128, 0, stream>>>(p);
+    SKV_CHECK_LAUNCH();
+    return SKV_OK;
+  }
   switch (L->kv_dtype) {
     case SKV_F32: return launch_prefill<float>(p, stream);
     case SKV_F16: return launch_prefill<__half>(p, stream);
