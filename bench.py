@@ -315,6 +315,90 @@ def cpu_step(oc, rng):
     oc._pending = sc
 
 
+E2E = dict(layers=16, hidden=2048, heads=32, kv_heads=8, head_dim=64, ffn=8192, theta=5e5, vocab=128256,
+           batch=32, prompt=8192, decode=256)
+
+
+def run_e2e(args, rank, world, dev):
+    """End-to-end decode through transformers: a Llama-3.2-1B-shaped decoder
+    (random N(0,0.02) weights, bf16) prefills 8192 random tokens per row and
+    greedily decodes 256 tokens with the windowed cache (budget 0.40, int4
+    tier).  The global batch of 32 rows is split across the ranks; decode
+    tokens/s = rows x steps / decode time (max over ranks), prefill excluded."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from stickykv_b200 import WindowedCache, WindowedCacheConfig, install_score_hooks
+
+    c = dict(E2E)
+    if args.e2e_prompt:
+        c["prompt"] = args.e2e_prompt
+    if args.e2e_decode:
+        c["decode"] = args.e2e_decode
+    rows = max(1, c["batch"] // world)
+    cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["ffn"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                      num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], rope_theta=c["theta"],
+                      max_position_embeddings=131072, tie_word_embeddings=True, initializer_range=0.02)
+    torch.manual_seed(1234 + rank)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    wcfg = WindowedCacheConfig(window_size=WS, num_sink_tokens=SINKS, local_window_size=LOCAL,
+                               cache_budget=BUDGET, int4_tier=True)
+    cache = WindowedCache(wcfg, c["prompt"], model.config, torch.bfloat16, model.model.rotary_emb,
+                          num_layers=c["layers"], max_tokens=c["decode"])
+    handles = install_score_hooks(model, cache, wcfg)
+    g = torch.Generator(device=dev).manual_seed(55 + rank)
+    ids = torch.randint(0, c["vocab"], (rows, c["prompt"]), device=dev, generator=g)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        p1.record(stream)
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        torch.cuda.synchronize(dev)
+        sampler = ClockSampler(dev.index if dev.index is not None else 0)
+        sampler.start()
+        time.sleep(0.3)
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(c["decode"] - 1):
+            out = model(input_ids=nxt, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop()
+    handles.remove()
+    t = torch.tensor([t0.elapsed_time(t1), p0.elapsed_time(p1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dec_ms, pre_ms = (float(x) for x in t.tolist())
+    if rank != 0:
+        return None
+    steps = c["decode"] - 1
+    total_rows = rows * world
+    return {
+        "metric": "e2e decode tokens/s (Llama-3.2-1B shape, 8k prompt, int4 tier)", "unit": "tokens/s",
+        "value": total_rows * steps / (dec_ms * 1e-3), "n_gpus": world, "steps": steps,
+        "ms_per_step": dec_ms / steps, "higher_is_better": True, "scaling": "strong",
+        "dtype": "bf16 (int4 tier codes)", "data": "synthetic: random N(0,0.02) weights, uniform token ids",
+        "config": {"workload": "Llama-3.2-1B-shaped decoder, greedy decode through transformers with the "
+                               "windowed cache", "layers": c["layers"], "hidden": c["hidden"],
+                   "q_heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
+                   "global_batch": total_rows, "prompt": c["prompt"], "decode_steps": c["decode"],
+                   "cache_budget": BUDGET, "retained_tokens": cache.get_seq_length(0),
+                   "parallelism": f"{world} batch shards"},
+        "prefill_ms": pre_ms, "clocks": clocks,
+    }
+
+
 def _all_host_threads():
     """BLAS thread pools sized to every host core (torchrun sets
     OMP_NUM_THREADS=1 for its ranks); returns (context, threads)."""
@@ -379,6 +463,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e", action="store_true",
+                    help="end-to-end decode through a Llama-3.2-1B-shaped transformers model instead")
+    ap.add_argument("--e2e-prompt", type=int, default=0)
+    ap.add_argument("--e2e-decode", type=int, default=0)
     ap.add_argument("--no-tier", action="store_true",
                     help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
     args = ap.parse_args()
@@ -399,7 +487,7 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     try:
-        line = run_ours(args, rank, world, dev)
+        line = run_e2e(args, rank, world, dev) if args.e2e else run_ours(args, rank, world, dev)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:
