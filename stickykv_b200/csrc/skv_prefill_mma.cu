@@ -4,19 +4,22 @@
 // Replaces the prefill branch of the flash score hook
 // (modules/windowed_cache/hooks.py:245-290: chunked softmax(q·kᵀ) with a
 // causal mask summed over the query rows, reduced to windows) together with
-// the prompt's attention, in two passes over 64x64 tiles:
-//   1. forward (flash-attention style): each block owns 64 query rows of one
-//      head, streams the key/value tiles at or below the diagonal through a
-//      cp.async double buffer and keeps an online softmax per row; it writes
-//      the output and the row's log-sum-exp (log2 domain).
-//   2. column mass: each block owns 64 keys, streams the query tiles at or
-//      above the diagonal and sums exp2(s - lse) over the rows of each key
-//      column (the same products as pass 1, transposed: S^T = K Q^T).
-// Both passes are mma.sync.m16n8k16 with fp32 accumulation; tiles live in
-// shared memory with the 16-byte chunk of row r stored at chunk ^ (r & 7),
-// which keeps every ldmatrix conflict-free.  The window reduction of the
-// column mass is the portable kernel's (skv_prefill.cu).
+// the prompt's attention, in two passes:
+//   1. forward (flash-attention style, mma.sync.m16n8k16): each block owns 64
+//      query rows of one head, streams the 64-key tiles at or below the
+//      diagonal through a cp.async double buffer and keeps an online softmax
+//      per row; it writes the output and the row's log-sum-exp (log2 domain).
+//      Tiles live in shared memory with the 16-byte chunk of row r stored at
+//      chunk ^ (r & 7), which keeps every ldmatrix conflict-free.
+//   2. column mass (the scoring contraction, tcgen05): each block owns 128
+//      keys, streams the 128-query tiles at or above the diagonal and sums
+//      exp2(s - lse) over the rows of each key column, S^T = K Q^T computed
+//      into tensor memory.
+// Both accumulate in fp32.  The window reduction of the column mass is the
+// portable kernel's (skv_prefill.cu).
 #include <float.h>
+
+#include <type_traits>
 
 #include "skv_mma.cuh"
 
@@ -36,7 +39,6 @@ template <int D> struct PCfg {
   static constexpr int kKB = D / 16;  // k-blocks over head_dim
   static constexpr int kDN = D / 8;   // 8-channel blocks of the output
   static constexpr size_t kFwdSmem = 5 * (size_t)kTileBytes;              // Q, K x2, V x2
-  static constexpr size_t kColSmem = 3 * (size_t)kTileBytes + 2 * kTile * 4;  // K, Q x2, lse x2
 };
 
 // 64 rows of a [T][D] matrix into a swizzled tile; rows >= T are zero-filled.
@@ -224,75 +226,203 @@ __global__ void __launch_bounds__(kPThreads) prefill_fwd_kernel(const PrefillPar
 }
 
 // ---------------------------------------------------------------------------
-// pass 2: column mass  colmass[j] = sum_{i >= j} exp2(s_ij - lse_i)
+// pass 2 on the 5th-generation tensor cores (tcgen05): S^T = K Q^T with
+// M = 128 keys, N = 128 queries, K = head_dim in 16-element steps, fp32
+// accumulators in tensor memory (two 128-column buffers: the MMA of the next
+// query tile runs while the warps read and exponentiate the current one).
+// Operands are K-major, 128-byte swizzled shared-memory tiles (8-row atoms of
+// 1 KiB; head_dim 128 is stored as two 64-channel halves).  One thread issues
+// the MMAs and commits them to an mbarrier; every thread owns one key row of
+// the accumulator.  Waits are bounded: a wait that runs out poisons the
+// block's column mass with NaN instead of hanging.
 // ---------------------------------------------------------------------------
+namespace tc {
+
+constexpr int kRows = 128;  // keys per block (MMA M) = queries per tile (MMA N)
+constexpr int kSpin = 1 << 24;
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                            // leading byte offset (16 B; unused when swizzled)
+  d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: 8-row atoms of 1 KiB
+  d |= (uint64_t)1 << 46;                            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                            // 128-byte swizzle
+  return d;
+}
+__host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |  // f32 accumulate, A/B type
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);          // K-major A and B
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+__device__ __forceinline__ void commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+__device__ __forceinline__ void bar_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar));
+}
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+  for (int it = 0; it < kSpin; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+__device__ __forceinline__ void ld32(uint32_t (&r)[32], uint32_t taddr) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// 128 rows x D of a [T][D] matrix into K-major 128-byte-swizzled halves of 64
+// channels (rows >= T zero-filled).
+template <int D>
+__device__ __forceinline__ void load_tile128(uint32_t dst, const void* src, int row0, int T) {
+  constexpr int CPR = D / 8;                  // 16-byte chunks per row
+  constexpr int HALF = kRows * 128;           // bytes of one 64-channel half
+  const unsigned char* base = static_cast<const unsigned char*>(src);
+  for (int idx = threadIdx.x; idx < kRows * CPR; idx += kPThreads) {
+    const int r = idx / CPR, c = idx % CPR, row = row0 + r;
+    const int h = c >> 3, cc = c & 7;
+    const unsigned char* s = base + ((int64_t)min(row, T - 1) * D + c * 8) * 2;
+    cp_async16_zfill(dst + h * HALF + r * 128 + ((cc ^ (r & 7)) * 16), s, row < T ? 16 : 0);
+  }
+}
+
+template <int D> struct TcCfg {
+  static constexpr int kTileBytes = kRows * D * 2;
+  // K tile, two query tiles, two lse rows, two mbarriers + TMEM address; sized
+  // so at most two blocks share an SM (2 x 256 TMEM columns)
+  static constexpr size_t kUsed = 3 * (size_t)kTileBytes + 2 * kRows * 4 + 64 + 1024;  // + alignment slack
+  static constexpr size_t kSmem = kUsed > 80 * 1024 ? kUsed : 80 * 1024;
+};
+
+}  // namespace tc
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kPThreads) prefill_colmass_kernel(const PrefillParams p) {
-  using C = PCfg<D>;
-  constexpr int KB = C::kKB;
-  extern __shared__ __align__(128) unsigned char smem[];
+__global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const PrefillParams p) {
+  using namespace tc;
+  using TC = TcCfg<D>;
+  constexpr bool kBF = !std::is_same<T, __half>::value;
+  constexpr uint32_t kIdesc = idesc_f16(kBF, kRows, kRows);
+  constexpr int KSTEPS = D / 16;
+  extern __shared__ __align__(128) unsigned char smem_tc[];
+  // swizzled operand tiles need 1 KiB alignment (the launch reserves the slack)
+  unsigned char* smem = smem_tc + ((1024 - (smem_u32(smem_tc) & 1023)) & 1023);
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.Hq / p.Hkv);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int k0 = kt * kTile;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k0 = kt * kRows;
   const T* qg = (const T*)p.q + ((int64_t)b * p.Hq + h) * p.T * D;
   const T* kg = (const T*)p.k + ((int64_t)b * p.Hkv + kh) * p.T * D;
   const float* lse = p.lse + ((int64_t)b * p.Hq + h) * p.T;
-  const uint32_t sK = smem_u32(smem), sQ = sK + C::kTileBytes;
-  float* sL = reinterpret_cast<float*>(smem + 3 * C::kTileBytes);  // [2][64]
+  const uint32_t sK = smem_u32(smem), sQ = sK + TC::kTileBytes;
+  float* sL = reinterpret_cast<float*>(smem + 3 * TC::kTileBytes);       // [2][128]
+  const uint32_t bars = smem_u32(smem + 3 * TC::kTileBytes + 2 * kRows * 4);  // 2 mbarriers
+  uint32_t* s_taddr = reinterpret_cast<uint32_t*>(smem + 3 * TC::kTileBytes + 2 * kRows * 4 + 16);
   const float sl2 = p.scaling * kLog2eP;
-  const int n_qt = (p.T + kTile - 1) / kTile;
+  const int n_qt = (p.T - k0 + kRows - 1) / kRows;  // query tiles at or above the diagonal
 
-  auto load_lse = [&](int buf, int qt) {
-    for (int i = threadIdx.x; i < kTile; i += kPThreads) {
-      const int row = qt * kTile + i;
-      sL[buf * kTile + i] = row < p.T ? lse[row] : INFINITY;  // rows past the end weigh 0
-    }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(smem_u32(s_taddr)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  if (threadIdx.x == 0) {
+    bar_init(bars);
+    bar_init(bars + 8);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  auto load_q = [&](int i) {  // query tile i of this block into buffer i & 1
+    const int q0 = k0 + i * kRows, buf = i & 1;
+    load_tile128<D>(sQ + buf * TC::kTileBytes, qg, q0, p.T);
+    const int row = q0 + threadIdx.x;  // kPThreads == kRows
+    sL[buf * kRows + threadIdx.x] = row < p.T ? lse[row] : INFINITY;  // rows past the end weigh 0
   };
-  load_tile<D>(sK, kg, k0, p.T);
-  load_tile<D>(sQ, qg, k0, p.T);
-  load_lse(0, kt);
-  cp_commit();
-
-  uint32_t ka[KB][4];
-  float cs[2] = {0.f, 0.f};                // column sums of keys g and g+8 of this warp
-  const int key_g = k0 + 16 * warp + g;
-  for (int qt = kt; qt < n_qt; ++qt) {
-    const int buf = (qt - kt) & 1;
-    if (qt + 1 < n_qt) {
-      load_tile<D>(sQ + (buf ^ 1) * C::kTileBytes, qg, (qt + 1) * kTile, p.T);
-      load_lse(buf ^ 1, qt + 1);
+  auto issue = [&](int i, uint32_t tmem) {  // S^T tile i into accumulator buffer i & 1
+    const uint32_t qb = sQ + (i & 1) * TC::kTileBytes;
+#pragma unroll
+    for (int k = 0; k < KSTEPS; ++k) {
+      const uint32_t off = (k >> 2) * (kRows * 128) + (k & 3) * 32;  // 64-channel half, 32 B per step
+      mma_f16(tmem + (i & 1) * kRows, desc_sw128(sK + off), desc_sw128(qb + off), kIdesc, k > 0 ? 1u : 0u);
     }
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    if (qt == kt) load_a<D>(ka, sK, 16 * warp);
-    float s[8][4];
+    commit(bars + 8 * (i & 1));
+  };
+
+  load_tile128<D>(sK, kg, k0, p.T);
+  load_q(0);
+  cp_commit();
+  if (n_qt > 1) load_q(1);
+  cp_commit();
+  cp_wait<1>();
+  fence_proxy_async();
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *s_taddr;
+  if (threadIdx.x == 0) issue(0, tmem);
+
+  bool lost = false;
+  float cs = 0.f;                        // column mass of this thread's key
+  const int key = k0 + 32 * warp + lane;  // accumulator row (tensor-memory lane)
+  for (int i = 0; i < n_qt; ++i) {
+    if (i + 1 < n_qt) {  // the next tile's MMA runs while this one is read
+      cp_wait<0>();
+      fence_proxy_async();
+      fence_before();
+      __syncthreads();
+      fence_after();
+      if (threadIdx.x == 0) issue(i + 1, tmem);
+    }
+    if (!bar_wait(bars + 8 * (i & 1), (i >> 1) & 1)) lost = true;
+    fence_after();
+    const int q0 = k0 + i * kRows;
+    const float* lt = sL + (i & 1) * kRows;
+    const uint32_t tacc = tmem + ((uint32_t)(32 * warp) << 16) + (i & 1) * kRows;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kRows; c0 += 32) {
+      uint32_t r[32];
+      ld32(r, tacc + c0);
+      ld_wait();
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
-    mma_rows<T, D>(s, ka, sQ + buf * C::kTileBytes);
-    const bool diag = qt == kt;
-    const int qbase = qt * kTile;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      const float2 lq = *reinterpret_cast<const float2*>(sL + buf * kTile + nb * 8 + 2 * t);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int qi = qbase + nb * 8 + 2 * t + (e & 1), key = key_g + 8 * (e >> 1);
-        float x = ex2(s[nb][e] * sl2 - ((e & 1) ? lq.y : lq.x));
-        if (diag && qi < key) x = 0.f;
-        cs[e >> 1] += x;
+      for (int j = 0; j < 32; ++j) {
+        const int q = q0 + c0 + j;
+        const float x = ex2(__uint_as_float(r[j]) * sl2 - lt[c0 + j]);
+        cs += (i == 0 && q < key) ? 0.f : x;
       }
     }
+    // every thread is done with accumulator i & 1 and query buffer i & 1
+    fence_before();
     __syncthreads();
+    fence_after();
+    if (i + 2 < n_qt) {
+      load_q(i + 2);
+    }
+    cp_commit();
   }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    cs[r] += __shfl_xor_sync(0xffffffffu, cs[r], 1);
-    cs[r] += __shfl_xor_sync(0xffffffffu, cs[r], 2);
-    const int key = key_g + 8 * r;
-    if (t == 0 && key < p.T) p.colmass[((int64_t)b * p.Hq + h) * p.T + key] = cs[r];
-  }
+  if (key < p.T) p.colmass[((int64_t)b * p.Hq + h) * p.T + key] = lost ? __int_as_float(0x7fc00000) : cs;
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem));
 }
 
 template <typename T, int D>
@@ -304,9 +434,11 @@ int launch(const PrefillParams& p, bool colmass, cudaStream_t stream) {
   prefill_fwd_kernel<T, D><<<grid, kPThreads, C::kFwdSmem, stream>>>(p);
   SKV_CHECK_LAUNCH();
   if (colmass) {
-    cudaFuncSetAttribute(prefill_colmass_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)C::kColSmem);
-    prefill_colmass_kernel<T, D><<<grid, kPThreads, C::kColSmem, stream>>>(p);
+    using TC = tc::TcCfg<D>;
+    cudaFuncSetAttribute(prefill_colmass_tc_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)TC::kSmem);
+    const dim3 g2((p.T + tc::kRows - 1) / tc::kRows, p.Hq, p.B);
+    prefill_colmass_tc_kernel<T, D><<<g2, kPThreads, TC::kSmem, stream>>>(p);
     SKV_CHECK_LAUNCH();
   }
   return SKV_OK;
