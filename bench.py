@@ -324,7 +324,8 @@ def run_e2e(args, rank, world, dev):
     (random N(0,0.02) weights, bf16) prefills 8192 random tokens per row and
     greedily decodes 256 tokens with the windowed cache (budget 0.40, int4
     tier).  The global batch of 32 rows is split across the ranks; decode
-    tokens/s = rows x steps / decode time (max over ranks), prefill excluded."""
+    tokens/s = rows x steps / decode time (max over ranks), prefill excluded.
+    At N > 1 the ranks all-gather each step's greedy tokens."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -366,10 +367,15 @@ def run_e2e(args, rank, world, dev):
         if world > 1:
             dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # every step the ranks gather the batch's next tokens (NCCL over NVLink),
+        # the only collective of the run; each rank keeps decoding its own rows
+        gathered = torch.empty(world * rows, 1, dtype=torch.long, device=dev) if world > 1 else None
         t0.record(stream)
         for _ in range(c["decode"] - 1):
             out = model(input_ids=nxt, past_key_values=cache, use_cache=True, logits_to_keep=1)
             nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+            if gathered is not None:
+                dist.all_gather_into_tensor(gathered, nxt)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
