@@ -23,6 +23,8 @@
 // pages (a block per page); scores and ids are gathered.
 #include <float.h>
 
+#include <type_traits>
+
 #include "skv_common.cuh"
 
 namespace skv {
@@ -340,7 +342,8 @@ __device__ void quantize_page_block(KF kin, VF vin, int pos0, const float* cos, 
 __host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D * 4 + 2 * 8 * D; }
 
 struct ApplyGrid {
-  int n_demote, n_gather, n_move;
+  int n_demote, n_gather, n_move, n_move_v;
+  int v_runs_per_row; // value-copy runs per row: the sinks and every kept fp window
   int demote_tasks;   // (candidate window, page) pairs per (row, kv head)
   int gather_chunks;  // kApplyThreads-window chunks per row
   int move_chunks;    // token chunks per row
@@ -394,8 +397,13 @@ __device__ void gather_block(const EvictParams& p, const ApplyGrid& a, int bid) 
 // KV dtype).  A thread owns one (token, 16-byte vector of the first half of
 // the channels) of one row and walks the KV heads, so its cos/sin rows are
 // loaded once; it handles the vector and its rotation partner.
+// Keys of the fp tokens that stay fp, stripped at the old and re-applied at
+// the new position (op by op in the KV dtype).  A thread owns one (token,
+// 16-byte vector of the first half of the channels) of one row and walks the
+// KV heads, so its cos/sin rows are loaded once; it handles the vector and
+// its rotation partner.
 template <typename T, int D>
-__device__ void move_block(const EvictParams& p, const ApplyGrid& a, int bid) {
+__device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) {
   constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr int half = D / 2, nvec = half / VE, tpb = kApplyThreads / nvec;
   const int b = bid / a.move_chunks, chunk = bid % a.move_chunks;
@@ -415,40 +423,128 @@ __device__ void move_block(const EvictParams& p, const ApplyGrid& a, int bid) {
   }
   const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
   const Geometry gn{p.s, p.s_pad, p.ws, p.T_new, p.n_tier_new_tok};
-  float co[VE], so[VE], cn[VE], sn[VE];
-#pragma unroll
-  for (int e = 0; e < VE; e += 4) {
-    *reinterpret_cast<float4*>(co + e) = *reinterpret_cast<const float4*>(p.cos + (int64_t)old_pos * half + c0 + e);
-    *reinterpret_cast<float4*>(so + e) = *reinterpret_cast<const float4*>(p.sin + (int64_t)old_pos * half + c0 + e);
-    *reinterpret_cast<float4*>(cn + e) = *reinterpret_cast<const float4*>(p.cos + (int64_t)new_pos * half + c0 + e);
-    *reinterpret_cast<float4*>(sn + e) = *reinterpret_cast<const float4*>(p.sin + (int64_t)new_pos * half + c0 + e);
-  }
   const int64_t so_slot = go.fp_slot(old_pos), sd_slot = gn.fp_slot(new_pos);
-  union Vec { uint4 u; T e[VE]; };
-#pragma unroll 1
-  for (int h = 0; h < p.Hkv; ++h) {
-    const int64_t rs = (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
-    const int64_t rd = (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
-    const T* ks = (const T*)p.k_src + rs;
-    const T* vs = (const T*)p.v_src + rs;
-    T* kd = (T*)p.k_dst + rd;
-    T* vd = (T*)p.v_dst + rd;
-    Vec kx, ky, ox, oy;
-    kx.u = *reinterpret_cast<const uint4*>(ks + c0);
-    ky.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
-    const uint4 v0 = *reinterpret_cast<const uint4*>(vs + c0);
-    const uint4 v1 = *reinterpret_cast<const uint4*>(vs + c0 + half);
+  const float* tco = p.cos + (int64_t)old_pos * half + c0;
+  const float* tso = p.sin + (int64_t)old_pos * half + c0;
+  const float* tcn = p.cos + (int64_t)new_pos * half + c0;
+  const float* tsn = p.sin + (int64_t)new_pos * half + c0;
+  if constexpr (sizeof(T) == 2) {
+    // fp16/bf16: an fp32 multiply or add of two KV-dtype values followed by a
+    // rounding to the KV dtype equals the dtype's own round-to-nearest
+    // multiply or add.  The fp32 product is exact; for the sum, fp32 carries
+    // at least 2p+2 significand bits of the p-bit dtype, which makes the
+    // double rounding innocuous (Figueroa, "When is double rounding
+    // innocuous?", SIGNUM 1995).  So the reference's op-by-op rounded strip
+    // and re-apply run as packed non-fused multiplies and adds, bit for bit.
+    using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+    T2 co[VE / 2], so[VE / 2], cn[VE / 2], sn[VE / 2];
 #pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      float x = Elt<T>::to_f32(kx.e[e]), y = Elt<T>::to_f32(ky.e[e]);
-      rope_strip_apply<T>(x, y, co[e], so[e], cn[e], sn[e]);
-      ox.e[e] = Elt<T>::from_f32(x);
-      oy.e[e] = Elt<T>::from_f32(y);
+    for (int e = 0; e < VE; e += 2) {
+      co[e / 2] = T2{Elt<T>::from_f32(tco[e]), Elt<T>::from_f32(tco[e + 1])};
+      so[e / 2] = T2{Elt<T>::from_f32(tso[e]), Elt<T>::from_f32(tso[e + 1])};
+      cn[e / 2] = T2{Elt<T>::from_f32(tcn[e]), Elt<T>::from_f32(tcn[e + 1])};
+      sn[e / 2] = T2{Elt<T>::from_f32(tsn[e]), Elt<T>::from_f32(tsn[e + 1])};
     }
-    *reinterpret_cast<uint4*>(kd + c0) = ox.u;
-    *reinterpret_cast<uint4*>(kd + c0 + half) = oy.u;
-    *reinterpret_cast<uint4*>(vd + c0) = v0;
-    *reinterpret_cast<uint4*>(vd + c0 + half) = v1;
+    union V2 { uint4 u; T2 e[VE / 2]; };
+#pragma unroll 1
+    for (int h = 0; h < p.Hkv; ++h) {
+      const T* ks = (const T*)p.k_src + (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
+      T* kd = (T*)p.k_dst + (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
+      V2 x, y;
+      x.u = *reinterpret_cast<const uint4*>(ks + c0);
+      y.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
+#pragma unroll
+      for (int e = 0; e < VE / 2; ++e) {
+        // strip (cos, -sin), then re-apply (cos, sin)
+        const T2 ux = __hadd2_rn(__hmul2_rn(x.e[e], co[e]), __hmul2_rn(y.e[e], so[e]));
+        const T2 uy = __hsub2_rn(__hmul2_rn(y.e[e], co[e]), __hmul2_rn(x.e[e], so[e]));
+        x.e[e] = __hsub2_rn(__hmul2_rn(ux, cn[e]), __hmul2_rn(uy, sn[e]));
+        y.e[e] = __hadd2_rn(__hmul2_rn(uy, cn[e]), __hmul2_rn(ux, sn[e]));
+      }
+      *reinterpret_cast<uint4*>(kd + c0) = x.u;
+      *reinterpret_cast<uint4*>(kd + c0 + half) = y.u;
+    }
+  } else {
+    float co[VE], so[VE], cn[VE], sn[VE];
+#pragma unroll
+    for (int e = 0; e < VE; e += 4) {
+      *reinterpret_cast<float4*>(co + e) = *reinterpret_cast<const float4*>(tco + e);
+      *reinterpret_cast<float4*>(so + e) = *reinterpret_cast<const float4*>(tso + e);
+      *reinterpret_cast<float4*>(cn + e) = *reinterpret_cast<const float4*>(tcn + e);
+      *reinterpret_cast<float4*>(sn + e) = *reinterpret_cast<const float4*>(tsn + e);
+    }
+    union Vec { uint4 u; T e[VE]; };
+#pragma unroll 1
+    for (int h = 0; h < p.Hkv; ++h) {
+      const T* ks = (const T*)p.k_src + (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
+      T* kd = (T*)p.k_dst + (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
+      Vec kx, ky, ox, oy;
+      kx.u = *reinterpret_cast<const uint4*>(ks + c0);
+      ky.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        float x = Elt<T>::to_f32(kx.e[e]), y = Elt<T>::to_f32(ky.e[e]);
+        rope_strip_apply<T>(x, y, co[e], so[e], cn[e], sn[e]);
+        ox.e[e] = Elt<T>::from_f32(x);
+        oy.e[e] = Elt<T>::from_f32(y);
+      }
+      *reinterpret_cast<uint4*>(kd + c0) = ox.u;
+      *reinterpret_cast<uint4*>(kd + c0 + half) = oy.u;
+    }
+  }
+}
+
+// Values of the fp tokens that stay fp: whole windows (and the sink rows) are
+// contiguous in both stores, so a block copies kVUnits runs of up to
+// window_size rows, 16 bytes per thread, with the run's offsets computed once
+// per run.
+constexpr int kVUnits = 4;
+template <typename T, int D>
+__device__ void move_v_block(const EvictParams& p, const ApplyGrid& a, int bid) {
+  constexpr int CPR = D * (int)sizeof(T) / 16;  // 16-byte chunks per row
+  const int per_unit = kApplyThreads / kVUnits;  // threads per run
+  const int unit = bid * kVUnits + threadIdx.x / per_unit;
+  const int b = unit / a.v_runs_per_row, run = unit % a.v_runs_per_row;
+  if (b >= p.B) return;
+  const int s_eff = min(p.s, p.T_old);
+  // run 0: the sinks; run 1 + j: kept window j of the fp region (tokens s_eff + 8j ...)
+  int tau0, rows;
+  if (run == 0) {
+    tau0 = 0;
+    rows = s_eff;
+  } else {
+    tau0 = s_eff + (run - 1) * p.ws;
+    rows = min(p.ws, a.n_fp_tok - tau0);
+  }
+  if (rows <= 0) return;
+  int old_pos, new_pos;
+  if (run == 0) {
+    old_pos = new_pos = 0;
+  } else {
+    const int jf = run - 1;
+    const int j = p.tier ? p.kprime + jf : jf;
+    const int w = p.tier ? p.E + jf : p.retained[(int64_t)b * p.R + j];
+    old_pos = p.s + w * p.ws;
+    new_pos = p.s + j * p.ws;
+  }
+  const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
+  const Geometry gn{p.s, p.s_pad, p.ws, p.T_new, p.n_tier_new_tok};
+  const int64_t so_slot = go.fp_slot(old_pos), sd_slot = gn.fp_slot(new_pos);
+  const int cw = rows * CPR;  // chunks of the run in one head
+  const int64_t hs_src = (int64_t)p.fp_cap_src * D, hs_dst = (int64_t)p.fp_cap_dst * D;
+  const T* src0 = (const T*)p.v_src + ((int64_t)b * p.Hkv * p.fp_cap_src + so_slot) * D;
+  T* dst0 = (T*)p.v_dst + ((int64_t)b * p.Hkv * p.fp_cap_dst + sd_slot) * D;
+  for (int c = threadIdx.x % per_unit; c < cw; c += per_unit) {
+    // all heads' loads first, then the stores (8 independent 16-byte loads in flight)
+    for (int h0 = 0; h0 < p.Hkv; h0 += 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (h0 + j < p.Hkv) v[j] = reinterpret_cast<const uint4*>(src0 + (h0 + j) * hs_src)[c];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (h0 + j < p.Hkv) reinterpret_cast<uint4*>(dst0 + (h0 + j) * hs_dst)[c] = v[j];
+    }
   }
 }
 
@@ -467,7 +563,12 @@ __global__ void __launch_bounds__(kApplyThreads, 3) evict_apply_kernel(EvictPara
     gather_block(p, a, bid);
     return;
   }
-  move_block<T, D>(p, a, bid - a.n_gather);
+  bid -= a.n_gather;
+  if (bid < a.n_move_v) {  // the short value copies first, then the key re-rotation
+    move_v_block<T, D>(p, a, bid);
+    return;
+  }
+  move_k_block<T, D>(p, a, bid - a.n_move_v);
 }
 
 template <typename T, int D>
@@ -500,7 +601,13 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
   constexpr int tpb = kApplyThreads / (D / 2 / (16 / (int)sizeof(T)));
   a.move_chunks = a.n_fp_tok > 0 ? ceil_div(a.n_fp_tok, tpb) : 0;
   a.n_move = a.move_chunks * p.B;
-  const int64_t blocks = (int64_t)a.n_demote + a.n_gather + a.n_move;
+  {
+    const int s_eff = min(p.s, p.T_old);
+    const int rest = a.n_fp_tok > s_eff ? a.n_fp_tok - s_eff : 0;
+    a.v_runs_per_row = a.n_fp_tok > 0 ? 1 + ceil_div(rest, p.ws) : 0;
+    a.n_move_v = ceil_div(a.v_runs_per_row * p.B, kVUnits);
+  }
+  const int64_t blocks = (int64_t)a.n_demote + a.n_gather + a.n_move + a.n_move_v;
   if (blocks == 0) return SKV_OK;
   if (blocks > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
   const size_t smem = a.n_demote ? quant_scratch_bytes(D) : 0;
