@@ -446,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       if (P != rq_pos) seed(P, p.scale_log2);
     }
     uint32_t cs = ring_s, is = ring_s + (SL - 1) * SB;
+#pragma unroll 2
     for (int i = i0; i < i1; ++i) {
       if (!can_step && i > i0) seed(p.s + 8 * (u0 + 2 * i - R.NS + (g >> 2)), p.scale_log2);
       if (i + SL - 1 < i1) issue(i + SL - 1, is + lane * 16);
