@@ -461,6 +461,45 @@ def run_reference(args, rank, world):
     }
 
 
+def run_tile_profile(dev):
+    """Two decode-attention calls on the steady cache cut to its int4 part (all
+    tier pages, then half of them) inside a profiler range: the difference of
+    their counters is the cost of the int4 tiles alone, fixed per-block costs
+    cancelling.  Run under `ncu --profile-from-start off`."""
+    import ctypes as C
+
+    import torch
+
+    from stickykv_b200 import _lib
+    cache = build_steady_cache(dev, 1, tier=True)
+    st = cache._states[0]
+    d = cache._desc(st, st.sides[st.cur])
+    L = _lib.lib()
+    q = torch.randn(B, HQ, D, device=dev, dtype=torch.float16)
+    out = torch.empty_like(q)
+    sc = torch.zeros(B, HQ, st.scores_cap, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    nb = L.skv_decode_workspace_size(C.byref(d), st.T)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    cases = [(SINKS + st.tier_pages * 8, st.tier_pages), (SINKS + (st.tier_pages // 2) * 8, st.tier_pages // 2)]
+
+    def call(T, tp):
+        _lib.check(L.skv_decode_attention(C.byref(d), T, tp, q.data_ptr(), q.stride(0), q.stride(1),
+                                          out.data_ptr(), out.stride(0), out.stride(1), C.c_float(D ** -0.5),
+                                          sc.data_ptr(), st.scores_cap, ws.data_ptr(), nb, s), "decode")
+
+    for T, tp in cases:
+        for _ in range(3):
+            call(T, tp)
+    torch.cuda.synchronize(dev)
+    torch.cuda.profiler.start()
+    for T, tp in cases:
+        call(T, tp)
+    torch.cuda.synchronize(dev)
+    torch.cuda.profiler.stop()
+    return {"tile_profile": [{"seq_len": T, "tier_pages": tp, "int4_tiles": B * HKV * (tp // 2)} for T, tp in cases]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -475,6 +514,8 @@ def main():
     ap.add_argument("--e2e-decode", type=int, default=0)
     ap.add_argument("--no-tier", action="store_true",
                     help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
+    ap.add_argument("--tile-profile", action="store_true",
+                    help="two decode calls on the int4 part of the cache in a profiler range (for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -493,7 +534,10 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     try:
-        line = run_e2e(args, rank, world, dev) if args.e2e else run_ours(args, rank, world, dev)
+        if args.tile_profile:
+            line = run_tile_profile(dev)
+        else:
+            line = run_e2e(args, rank, world, dev) if args.e2e else run_ours(args, rank, world, dev)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:
