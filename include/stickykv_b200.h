@@ -216,7 +216,8 @@ int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_ev
 
 /*
  * Prefill: causal attention of q [batch][num_q_heads][T][head_dim] over
- * k/v [batch][num_kv_heads][T][head_dim] (all kv_dtype, contiguous) ->
+ * k/v [batch][num_kv_heads][T][head_dim] (all kv_dtype, contiguous, 16-byte
+ * aligned like out; else SKV_ERR_MISALIGNED) ->
  * out [batch][T][num_q_heads][head_dim], and window_scores[b,h,w] += the
  * column mass of window w summed over all T query rows.
  */

@@ -282,6 +282,7 @@ int skv_prefill_attention(const skv_layer_desc* L, int32_t T, const void* q, con
   int rc = check_layer(L);
   if (rc) return rc;
   if (T <= 0 || !q || !k || !v || !out) return SKV_ERR_INVALID_ARG;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16)) return SKV_ERR_MISALIGNED;
   const Geometry g = geometry(L, T, 0);
   if (scores && scores_cap < g.num_windows()) return SKV_ERR_CAPACITY;
   if (!ws || ws_bytes < skv_prefill_workspace_size(L, T)) return SKV_ERR_WORKSPACE;

@@ -1,18 +1,18 @@
 // Tensor-core prefill: causal attention of the prompt and its column mass
-// (fp16/bf16, head_dim 64 or 128, any GQA ratio).
+// (fp16/bf16, head_dim 64 or 128, any GQA ratio), both on the 5th-generation
+// tensor cores (tcgen05, accumulators in tensor memory).
 //
 // Replaces the prefill branch of the flash score hook
 // (modules/windowed_cache/hooks.py:245-290: chunked softmax(q·kᵀ) with a
 // causal mask summed over the query rows, reduced to windows) together with
 // the prompt's attention, in two passes:
-//   1. forward (flash-attention style, mma.sync.m16n8k16): each block owns 64
-//      query rows of one head, streams the 64-key tiles at or below the
-//      diagonal through a cp.async double buffer and keeps an online softmax
-//      per row; it writes the output and the row's log-sum-exp (log2 domain).
-//      Tiles live in shared memory with the 16-byte chunk of row r stored at
-//      chunk ^ (r & 7), which keeps every ldmatrix conflict-free.
-//   2. column mass (the scoring contraction, tcgen05): each block owns 128
-//      keys, streams the 128-query tiles at or above the diagonal and sums
+//   1. forward (flash-attention style): each block owns 128 query rows of one
+//      head and streams the 128-key tiles at or below the diagonal; S = Q Kᵀ
+//      and O += P V are tcgen05 MMAs, the online softmax runs on the CUDA
+//      cores between them; it writes the output and the row's log-sum-exp
+//      (log2 domain).
+//   2. column mass (the scoring contraction): each block owns 128 keys,
+//      streams the 128-query tiles at or above the diagonal and sums
 //      exp2(s - lse) over the rows of each key column, S^T = K Q^T computed
 //      into tensor memory.
 // Both accumulate in fp32.  The window reduction of the column mass is the
@@ -28,202 +28,8 @@ namespace {
 
 using namespace mma;
 
-constexpr int kTile = 64;        // rows (queries or keys) per tile
-constexpr int kPThreads = 128;   // 4 warps x 16 rows
+constexpr int kPThreads = 128;   // threads of the scoring kernel: one key row each
 constexpr float kLog2eP = 1.4426950408889634f;
-
-template <int D> struct PCfg {
-  static constexpr int kRowBytes = 2 * D;
-  static constexpr int kTileBytes = kTile * kRowBytes;
-  static constexpr int kCPR = D / 8;  // 16-byte chunks per row
-  static constexpr int kKB = D / 16;  // k-blocks over head_dim
-  static constexpr int kDN = D / 8;   // 8-channel blocks of the output
-  static constexpr size_t kFwdSmem = 5 * (size_t)kTileBytes;              // Q, K x2, V x2
-};
-
-// 64 rows of a [T][D] matrix into a swizzled tile; rows >= T are zero-filled.
-template <int D>
-__device__ __forceinline__ void load_tile(uint32_t dst, const void* src, int row0, int T) {
-  using C = PCfg<D>;
-  const unsigned char* base = static_cast<const unsigned char*>(src);
-  for (int idx = threadIdx.x; idx < kTile * C::kCPR; idx += kPThreads) {
-    const int r = idx / C::kCPR, c = idx % C::kCPR, row = row0 + r;
-    const unsigned char* s = base + ((int64_t)min(row, T - 1) * D + c * 8) * 2;
-    cp_async16_zfill(dst + r * C::kRowBytes + ((c ^ (r & 7)) * 16), s, row < T ? 16 : 0);
-  }
-}
-
-// A fragments (m16 x k16, row-major) of rows [r0, r0+16) of a swizzled tile
-template <int D>
-__device__ __forceinline__ void load_a(uint32_t (&a)[D / 16][4], uint32_t tile, int r0) {
-  using C = PCfg<D>;
-  const int lane = threadIdx.x & 31, m = lane >> 3;
-  const int r = r0 + (m & 1) * 8 + (lane & 7);
-#pragma unroll
-  for (int kb = 0; kb < C::kKB; ++kb) {
-    const int c = 2 * kb + (m >> 1);
-    ldsm_x4(a[kb][0], a[kb][1], a[kb][2], a[kb][3], tile + r * C::kRowBytes + ((c ^ (r & 7)) * 16));
-  }
-}
-
-// acc[nb] += A (16 x D) . B^T for the 64 rows of a swizzled tile used as the
-// B operand (B[k = channel][n = tile row]), n-blocks of 8 rows
-template <typename T, int D>
-__device__ __forceinline__ void mma_rows(float (&acc)[8][4], const uint32_t (&a)[D / 16][4], uint32_t tile) {
-  using C = PCfg<D>;
-  using O = Op<T>;
-  const int lane = threadIdx.x & 31, m = lane >> 3;
-#pragma unroll
-  for (int kb = 0; kb < C::kKB; ++kb)
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      const int r = (2 * np + (m >> 1)) * 8 + (lane & 7), c = 2 * kb + (m & 1);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(b0, b1, b2, b3, tile + r * C::kRowBytes + ((c ^ (r & 7)) * 16));
-      O::mma(acc[2 * np], a[kb][0], a[kb][1], a[kb][2], a[kb][3], b0, b1);
-      O::mma(acc[2 * np + 1], a[kb][0], a[kb][1], a[kb][2], a[kb][3], b2, b3);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// pass 1: output and log-sum-exp
-// ---------------------------------------------------------------------------
-template <typename T, int D>
-__global__ void __launch_bounds__(kPThreads) prefill_fwd_kernel(const PrefillParams p) {
-  using C = PCfg<D>;
-  using O = Op<T>;
-  constexpr int KB = C::kKB, DN = C::kDN;
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int qt = gridDim.x - 1 - blockIdx.x;  // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int kh = h / (p.Hq / p.Hkv);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int q0 = qt * kTile;
-  const T* qg = (const T*)p.q + ((int64_t)b * p.Hq + h) * p.T * D;
-  const T* kg = (const T*)p.k + ((int64_t)b * p.Hkv + kh) * p.T * D;
-  const T* vg = (const T*)p.v + ((int64_t)b * p.Hkv + kh) * p.T * D;
-  const uint32_t sQ = smem_u32(smem), sK = sQ + C::kTileBytes, sV = sK + 2 * C::kTileBytes;
-  const float sl2 = p.scaling * kLog2eP;
-
-  load_tile<D>(sQ, qg, q0, p.T);
-  load_tile<D>(sK, kg, 0, p.T);
-  load_tile<D>(sV, vg, 0, p.T);
-  cp_commit();
-
-  uint32_t qa[KB][4];
-  float o[DN][4];
-#pragma unroll
-  for (int dn = 0; dn < DN; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  const int row_g = q0 + 16 * warp + g;  // query index of accumulator rows g and g+8
-  const int n_kt = qt + 1;               // key tiles at or below the diagonal
-
-  for (int kt = 0; kt < n_kt; ++kt) {
-    const int buf = kt & 1;
-    if (kt + 1 < n_kt) {
-      load_tile<D>(sK + (buf ^ 1) * C::kTileBytes, kg, (kt + 1) * kTile, p.T);
-      load_tile<D>(sV + (buf ^ 1) * C::kTileBytes, vg, (kt + 1) * kTile, p.T);
-    }
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    if (kt == 0) load_a<D>(qa, sQ, 16 * warp);
-
-    float s[8][4];
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
-    mma_rows<T, D>(s, qa, sK + buf * C::kTileBytes);
-
-    // scale into the log2 domain; causal and sequence-end masks
-    const int k0 = kt * kTile;
-    const bool edge = kt == qt || k0 + kTile > p.T;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float x = s[nb][e] * sl2;
-        if (edge) {
-          const int key = k0 + nb * 8 + 2 * t + (e & 1), row = row_g + 8 * (e >> 1);
-          if (key > row || key >= p.T) x = -INFINITY;
-        }
-        s[nb][e] = x;
-      }
-    // online softmax per row (rows g and g+8 of this warp)
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      mx[0] = fmaxf(mx[0], fmaxf(s[nb][0], s[nb][1]));
-      mx[1] = fmaxf(mx[1], fmaxf(s[nb][2], s[nb][3]));
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-    }
-    float alpha[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const float mn = fmaxf(m_run[r], mx[r]);
-      alpha[r] = mn == -INFINITY ? 1.f : ex2(m_run[r] - mn);
-      m_run[r] = mn;
-    }
-    float rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      s[nb][0] = m_run[0] == -INFINITY ? 0.f : ex2(s[nb][0] - m_run[0]);
-      s[nb][1] = m_run[0] == -INFINITY ? 0.f : ex2(s[nb][1] - m_run[0]);
-      s[nb][2] = m_run[1] == -INFINITY ? 0.f : ex2(s[nb][2] - m_run[1]);
-      s[nb][3] = m_run[1] == -INFINITY ? 0.f : ex2(s[nb][3] - m_run[1]);
-      rs[0] += s[nb][0] + s[nb][1];
-      rs[1] += s[nb][2] + s[nb][3];
-    }
-    l_run[0] = l_run[0] * alpha[0] + rs[0];
-    l_run[1] = l_run[1] * alpha[1] + rs[1];
-#pragma unroll
-    for (int dn = 0; dn < DN; ++dn) {
-      o[dn][0] *= alpha[0]; o[dn][1] *= alpha[0];
-      o[dn][2] *= alpha[1]; o[dn][3] *= alpha[1];
-    }
-    // O += P V: P's accumulator layout is the A layout of the next MMA
-    const uint32_t vt = sV + buf * C::kTileBytes;
-    const int m = lane >> 3;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t a0 = O::pack(s[2 * kk][0], s[2 * kk][1]);
-      const uint32_t a1 = O::pack(s[2 * kk][2], s[2 * kk][3]);
-      const uint32_t a2 = O::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      const uint32_t a3 = O::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-      const int r = 16 * kk + (m & 1) * 8 + (lane & 7);
-#pragma unroll
-      for (int dp = 0; dp < DN / 2; ++dp) {
-        const int c = 2 * dp + (m >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(b0, b1, b2, b3, vt + r * C::kRowBytes + ((c ^ (r & 7)) * 16));
-        O::mma(o[2 * dp], a0, a1, a2, a3, b0, b1);
-        O::mma(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
-      }
-    }
-    __syncthreads();  // the buffer just read is refilled next iteration
-  }
-
-  // finalise: totals over the 4 lanes of a row
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
-  }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = row_g + 8 * r;
-    if (row >= p.T) continue;
-    const float inv = 1.f / l_run[r];
-    T* orow = (T*)p.out + (((int64_t)b * p.T + row) * p.Hq + h) * D;
-#pragma unroll
-    for (int dn = 0; dn < DN; ++dn)
-      *reinterpret_cast<uint32_t*>(orow + dn * 8 + 2 * t) = O::pack(o[dn][2 * r] * inv, o[dn][2 * r + 1] * inv);
-    if (t == 0) p.lse[((int64_t)b * p.Hq + h) * p.T + row] = m_run[r] + __log2f(l_run[r]);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // pass 2 on the 5th-generation tensor cores (tcgen05): S^T = K Q^T with
@@ -292,15 +98,37 @@ __device__ __forceinline__ void ld32(uint32_t (&r)[32], uint32_t taddr) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// MN-major 128-byte-swizzled operand: rows of 64 MN elements (128 B), 8-row
+// atoms of 1 KiB along K (stride byte offset), 64-element column blocks
+// `lbo` bytes apart along MN (leading byte offset)
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t addr, uint32_t lbo) {
+  uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
 
 // 128 rows x D of a [T][D] matrix into K-major 128-byte-swizzled halves of 64
 // channels (rows >= T zero-filled).
-template <int D>
+template <int D, int NT = kPThreads>
 __device__ __forceinline__ void load_tile128(uint32_t dst, const void* src, int row0, int T) {
   constexpr int CPR = D / 8;                  // 16-byte chunks per row
   constexpr int HALF = kRows * 128;           // bytes of one 64-channel half
   const unsigned char* base = static_cast<const unsigned char*>(src);
-  for (int idx = threadIdx.x; idx < kRows * CPR; idx += kPThreads) {
+  for (int idx = threadIdx.x; idx < kRows * CPR; idx += NT) {
     const int r = idx / CPR, c = idx % CPR, row = row0 + r;
     const int h = c >> 3, cc = c & 7;
     const unsigned char* s = base + ((int64_t)min(row, T - 1) * D + c * 8) * 2;
@@ -425,13 +253,240 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem));
 }
 
+// ---------------------------------------------------------------------------
+// pass 1 on tcgen05: each block owns 128 query rows of one head.  Per 128-key
+// tile at or below the diagonal:
+//   S = Q K^T into tensor memory (M = 128 queries, N = 128 keys, K-major
+//     operands);
+//   two threads per query row (warps w and w + 4 share a lane quarter and
+//     take key columns 0-63 and 64-127) read their half of the row once, after
+//     which the next tile's QK MMA is issued; they exchange the half-row
+//     maxima, keep an online softmax whose running max
+//     moves only when the row max exceeds it by more than 8 (log2 domain; then
+//     the row of O is rescaled in tensor memory), and write P (KV dtype) into
+//     a K-major swizzled shared tile;
+//   one thread issues O += P V into a second accumulator (B = the V tile,
+//     MN-major: keys run down its 128-byte rows).
+// K tiles are fetched two tiles ahead and V tiles one ahead (cp.async double
+// buffers); the MMAs of the next tile run while the threads wait.  Waits are
+// bounded: one that runs out poisons the block's output with NaN.
+// ---------------------------------------------------------------------------
+constexpr int kFThreads = 256;
+
+template <int D> struct FwdTcCfg {
+  static constexpr int kTileBytes = tc::kRows * D * 2;         // Q, K or V tile
+  static constexpr int kPBytes = tc::kRows * tc::kRows * 2;   // P tile
+  // Q, K x2, V x2, P, half-row maxima/sums, mbarriers + TMEM address, 1 KiB slack
+  static constexpr size_t kSmem = 5 * (size_t)kTileBytes + kPBytes + 2 * tc::kRows * 4 + 64 + 1024;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_kernel(const PrefillParams p) {
+  using namespace tc;
+  using FC = FwdTcCfg<D>;
+  using O = Op<T>;
+  constexpr bool kBF = !std::is_same<T, __half>::value;
+  constexpr uint32_t kIdescS = idesc_f16(kBF, kRows, kRows);
+  constexpr uint32_t kIdescO = idesc_f16(kBF, kRows, D) | (1u << 16);  // B (V) MN-major
+  constexpr int KS = D / 16;                  // QK steps over head_dim
+  constexpr int KP = kRows / 16;              // PV steps over the key tile
+  constexpr int HALF = kRows * 128;           // one 64-element column block of a tile
+  constexpr uint32_t kOcol = kRows;           // O accumulator columns [128, 128 + D)
+  constexpr int OC = D / 2;                   // O columns per thread
+  constexpr float kThresh = 8.f;
+  extern __shared__ __align__(128) unsigned char smem_tc[];
+  unsigned char* smem = smem_tc + ((1024 - (smem_u32(smem_tc) & 1023)) & 1023);
+  const int qt = gridDim.x - 1 - blockIdx.x;  // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (p.Hq / p.Hkv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int rl = 32 * quarter + lane;         // tile row (tensor-memory lane)
+  const int q0 = qt * kRows;
+  const int row = q0 + rl;                    // this thread's query
+  const T* qg = (const T*)p.q + ((int64_t)b * p.Hq + h) * p.T * D;
+  const T* kg = (const T*)p.k + ((int64_t)b * p.Hkv + kh) * p.T * D;
+  const T* vg = (const T*)p.v + ((int64_t)b * p.Hkv + kh) * p.T * D;
+  const uint32_t sQ = smem_u32(smem), sK = sQ + FC::kTileBytes, sV = sK + 2 * FC::kTileBytes;
+  const uint32_t sP = sV + 2 * FC::kTileBytes;
+  float* xch = reinterpret_cast<float*>(smem + 5 * FC::kTileBytes + FC::kPBytes);  // [2][128]
+  const uint32_t bars = sP + FC::kPBytes + 2 * kRows * 4;  // barS, barPV
+  uint32_t* s_taddr = reinterpret_cast<uint32_t*>(smem + 5 * FC::kTileBytes + FC::kPBytes + 2 * kRows * 4 + 16);
+  const float sl2 = p.scaling * kLog2eP;
+  const int n_kt = qt + 1;  // key tiles at or below the diagonal
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(smem_u32(s_taddr)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  if (threadIdx.x == 0) {
+    bar_init(bars);
+    bar_init(bars + 8);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  auto issue_s = [&](int j, uint32_t tmem) {  // S = Q K_j^T
+    const uint32_t kb = sK + (j & 1) * FC::kTileBytes;
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+      const uint32_t off = (k >> 2) * HALF + (k & 3) * 32;
+      mma_f16(tmem, desc_sw128(sQ + off), desc_sw128(kb + off), kIdescS, k > 0 ? 1u : 0u);
+    }
+    commit(bars);
+  };
+  auto issue_pv = [&](int j, uint32_t tmem) {  // O += P V_j
+    const uint32_t vb = sV + (j & 1) * FC::kTileBytes;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      const uint32_t offp = (k >> 2) * HALF + (k & 3) * 32;
+      mma_f16(tmem + kOcol, desc_sw128(sP + offp), desc_sw128_mn(vb + k * 16 * 128, HALF), kIdescO,
+              (j > 0 || k > 0) ? 1u : 0u);
+    }
+    commit(bars + 8);
+  };
+  // the two threads of a row meet at named barrier 1 + quarter (warps w, w + 4)
+  auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;\n" ::"r"(1 + quarter) : "memory"); };
+
+  // cp.async groups: {Q, K_0}, {K_1}, {V_0}, then per tile j {K_j+2}, {V_j+1}
+  load_tile128<D, kFThreads>(sQ, qg, q0, p.T);
+  load_tile128<D, kFThreads>(sK, kg, 0, p.T);
+  cp_commit();
+  if (n_kt > 1) load_tile128<D, kFThreads>(sK + FC::kTileBytes, kg, kRows, p.T);
+  cp_commit();
+  load_tile128<D, kFThreads>(sV, vg, 0, p.T);
+  cp_commit();
+  cp_wait<2>();
+  fence_proxy_async();
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *s_taddr;
+  const uint32_t trow = tmem + ((uint32_t)(32 * quarter) << 16);  // this warp's lane quarter
+  const uint32_t tS = trow + 64 * half, tO = trow + kOcol + OC * half;
+  if (threadIdx.x == 0) issue_s(0, tmem);
+
+  bool lost = false;
+  float m_run = -INFINITY, m_thr = -INFINITY, l_run = 0.f;
+  for (int j = 0; j < n_kt; ++j) {
+    const int k0 = j * kRows + 64 * half;           // first key of this thread's columns
+    const bool edge = j == qt || k0 + 64 > p.T;     // causal diagonal or sequence end
+    if (!bar_wait(bars, j & 1)) lost = true;        // S_j in tensor memory
+    fence_after();
+    uint32_t r[64];
+    ld32(*reinterpret_cast<uint32_t(*)[32]>(r), tS);
+    ld32(*reinterpret_cast<uint32_t(*)[32]>(r + 32), tS + 32);
+    if (j + 2 < n_kt) load_tile128<D, kFThreads>(sK + (j & 1) * FC::kTileBytes, kg, (j + 2) * kRows, p.T);
+    cp_commit();
+    ld_wait();
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      float x = __uint_as_float(r[i]) * sl2;
+      if (edge && (k0 + i > row || k0 + i >= p.T)) x = -INFINITY;
+      r[i] = __float_as_uint(x);
+      mx = fmaxf(mx, x);
+    }
+    xch[half * kRows + rl] = mx;
+    // every thread has read S_j and K_{j+1} is resident: the next QK MMA
+    // runs during the rest of this tile
+    cp_wait<2>();
+    fence_proxy_async();
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (threadIdx.x == 0 && j + 1 < n_kt) issue_s(j + 1, tmem);
+    mx = fmaxf(mx, xch[(half ^ 1) * kRows + rl]);
+    // PV_{j-1} done: P, V_{j-1} and O are free
+    if (j > 0 && !bar_wait(bars + 8, (j - 1) & 1)) lost = true;
+    fence_after();
+    if (j + 1 < n_kt) load_tile128<D, kFThreads>(sV + ((j + 1) & 1) * FC::kTileBytes, vg, (j + 1) * kRows, p.T);
+    cp_commit();
+    // lazy rescale: the running max moves only by more than kThresh
+    const bool need = mx > m_thr;
+    if (__any_sync(0xffffffffu, need)) {
+      const float mn = need ? mx : m_run;
+      const float alpha = !need ? 1.f : (m_run == -INFINITY ? 0.f : ex2(m_run - mn));
+      l_run *= alpha;
+      m_run = mn;
+      m_thr = mn + kThresh;
+      if (j > 0) {  // this thread's half of its O row
+#pragma unroll 1
+        for (int c0 = 0; c0 < OC; c0 += 32) {
+          uint32_t o[32];
+          ld32(o, tO + c0);
+          ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          st32(tO + c0, o);
+        }
+        st_wait();
+      }
+    }
+    // P = exp2(s - m) into this thread's half of the swizzled P row, row sum
+    float rs = 0.f;
+    const int r7 = rl & 7;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {  // 16-byte chunks of 8 keys
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x0 = ex2(__uint_as_float(r[8 * c + 2 * e]) - m_run);
+        const float x1 = ex2(__uint_as_float(r[8 * c + 2 * e + 1]) - m_run);
+        rs += x0 + x1;
+        pk[e] = O::pack(x0, x1);
+      }
+      const uint32_t dst = sP + half * HALF + rl * 128 + ((c ^ r7) * 16);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(dst), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]),
+                   "r"(pk[3])
+                   : "memory");
+    }
+    l_run += rs;
+    // V_j resident, P complete
+    cp_wait<2>();
+    fence_proxy_async();
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (threadIdx.x == 0) issue_pv(j, tmem);
+  }
+  if (!bar_wait(bars + 8, (n_kt - 1) & 1)) lost = true;
+  fence_after();
+  xch[half * kRows + rl] = l_run;
+  pair_sync();
+  const float l_row = l_run + xch[(half ^ 1) * kRows + rl];
+  // O / l into this thread's half of the output row; log-sum-exp
+  const float inv = lost ? __int_as_float(0x7fc00000) : 1.f / l_row;
+  T* orow = (T*)p.out + (((int64_t)b * p.T + row) * p.Hq + h) * D + OC * half;
+#pragma unroll 1
+  for (int c0 = 0; c0 < OC; c0 += 32) {
+    uint32_t o[32];
+    ld32(o, tO + c0);
+    ld_wait();
+    if (row < p.T) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 v;
+        v.x = O::pack(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+        v.y = O::pack(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+        v.z = O::pack(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+        v.w = O::pack(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+        *reinterpret_cast<uint4*>(orow + c0 + 8 * q) = v;
+      }
+    }
+  }
+  if (row < p.T && half == 0)
+    p.lse[((int64_t)b * p.Hq + h) * p.T + row] = lost ? __int_as_float(0x7fc00000) : m_run + __log2f(l_row);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem));
+}
+
 template <typename T, int D>
 int launch(const PrefillParams& p, bool colmass, cudaStream_t stream) {
-  using C = PCfg<D>;
-  const int tiles = (p.T + kTile - 1) / kTile;
-  const dim3 grid(tiles, p.Hq, p.B);
-  cudaFuncSetAttribute(prefill_fwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kFwdSmem);
-  prefill_fwd_kernel<T, D><<<grid, kPThreads, C::kFwdSmem, stream>>>(p);
+  using FC = FwdTcCfg<D>;
+  const dim3 grid((p.T + tc::kRows - 1) / tc::kRows, p.Hq, p.B);
+  cudaFuncSetAttribute(prefill_fwd_tc_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FC::kSmem);
+  prefill_fwd_tc_kernel<T, D><<<grid, kFThreads, FC::kSmem, stream>>>(p);
   SKV_CHECK_LAUNCH();
   if (colmass) {
     using TC = tc::TcCfg<D>;
