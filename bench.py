@@ -195,7 +195,9 @@ def run_ours(args, rank, world, dev):
     n_evict = sum(1 for s in range(step0, step0 + args.steps) if s > 0 and s % WS == 0)
     # e2e: the same step through the public API with host buffers inside the
     # timed region: one pinned H2D copy of this step's packed q|k|v at the
-    # start of the step, one D2H copy of the attention output at its end
+    # start of the step on the compute stream, one D2H copy of the attention
+    # output on a copy stream (it overlaps the next step; the timed region
+    # ends after the last copy)
     nq_el, nk_el = B * HQ * D, B * HKV * D
     hin = torch.randn(nq, nq_el + 2 * nk_el, generator=torch.Generator().manual_seed(7),
                       dtype=torch.float16).pin_memory()
@@ -205,12 +207,17 @@ def run_ours(args, rank, world, dev):
     dk = din[nq_el:nq_el + nk_el].view(B, HKV, 1, D)
     dv = din[nq_el + nk_el:].view(B, HKV, 1, D)
 
+    copy_stream = torch.cuda.Stream(dev)
+
     def e2e_step(i):
         j = i % nq
         din.copy_(hin[j], non_blocking=True)
         cache.update(dk, dv, 0)
         out = cache.decode_attention(0, dq, scale)
-        hout[j].copy_(out, non_blocking=True)
+        copy_stream.wait_stream(stream)
+        with torch.cuda.stream(copy_stream):
+            hout[j].copy_(out, non_blocking=True)
+        out.record_stream(copy_stream)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -221,6 +228,7 @@ def run_ours(args, rank, world, dev):
     e0.record(stream)
     for i in range(args.steps):
         e2e_step(i)
+    stream.wait_stream(copy_stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
@@ -500,6 +508,57 @@ def run_tile_profile(dev):
     return {"tile_profile": [{"seq_len": T, "tier_pages": tp, "int4_tiles": B * HKV * (tp // 2)} for T, tp in cases]}
 
 
+def run_prefill(args, dev):
+    """Prompt prefill through the C-ABI (`skv_prefill_attention`: causal
+    attention, log-sum-exp and the prompt's window scores) on synthetic bf16
+    q/k/v, timed with CUDA events; TFLOP/s counts three causal GEMMs (QK and
+    PV of the forward, QK again for the column mass)."""
+    import ctypes as C
+
+    import torch
+
+    from stickykv_b200 import _lib
+    L = _lib.lib()
+    Bp, T, Dp = args.prefill_batch, args.prefill_len, args.prefill_head_dim
+    g = torch.Generator(device=dev).manual_seed(3)
+    dt = torch.bfloat16
+    q = torch.randn(Bp, HQ, T, Dp, device=dev, dtype=dt, generator=g)
+    k = torch.randn(Bp, HKV, T, Dp, device=dev, dtype=dt, generator=g)
+    v = torch.randn(Bp, HKV, T, Dp, device=dev, dtype=dt, generator=g)
+    out = torch.empty(Bp, T, HQ, Dp, device=dev, dtype=dt)
+    W = -(-(T - SINKS) // WS)
+    sc = torch.zeros(Bp, HQ, W + 8, device=dev)
+    d = _lib.LayerDesc()
+    d.batch, d.num_kv_heads, d.num_q_heads, d.head_dim = Bp, HKV, HQ, Dp
+    d.kv_dtype, d.window_size, d.num_sink, d.sink_pad = 2, WS, SINKS, 8
+    d.fp_capacity, d.k_fp, d.v_fp = T, k.data_ptr(), v.data_ptr()
+    nb = L.skv_prefill_workspace_size(C.byref(d), T)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+
+    def call():
+        _lib.check(L.skv_prefill_attention(C.byref(d), T, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                           out.data_ptr(), C.c_float(Dp ** -0.5), sc.data_ptr(), sc.shape[-1],
+                                           ws.data_ptr(), nb, s), "prefill")
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    flop = 3 * 2 * Bp * HQ * T * T * Dp / 2
+    return {"metric": "prefill TFLOP/s (causal attention + column-mass scoring, 3 causal GEMMs)",
+            "value": flop / ms / 1e9, "unit": "TFLOP/s", "ms_per_call": ms, "steps": args.steps,
+            "warmup": args.warmup, "dtype": "bf16", "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "prompt prefill", "batch": Bp, "q_heads": HQ, "kv_heads": HKV,
+                       "head_dim": Dp, "prompt": T}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -516,6 +575,10 @@ def main():
                     help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
     ap.add_argument("--tile-profile", action="store_true",
                     help="two decode calls on the int4 part of the cache in a profiler range (for ncu)")
+    ap.add_argument("--prefill", action="store_true", help="time the prompt prefill kernels instead")
+    ap.add_argument("--prefill-batch", type=int, default=4)
+    ap.add_argument("--prefill-len", type=int, default=8192)
+    ap.add_argument("--prefill-head-dim", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -536,6 +599,8 @@ def main():
     try:
         if args.tile_profile:
             line = run_tile_profile(dev)
+        elif args.prefill:
+            line = run_prefill(args, dev)
         else:
             line = run_e2e(args, rank, world, dev) if args.e2e else run_ours(args, rank, world, dev)
         if line is not None:

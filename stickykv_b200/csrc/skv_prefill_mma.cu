@@ -109,6 +109,14 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 __device__ __forceinline__ void st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld1(uint32_t taddr) {
+  uint32_t v;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n" : "=r"(v) : "r"(taddr));
+  return v;
+}
 // MN-major 128-byte-swizzled operand: rows of 64 MN elements (128 B), 8-row
 // atoms of 1 KiB along K (stride byte offset), 64-element column blocks
 // `lbo` bytes apart along MN (leading byte offset)
@@ -276,8 +284,14 @@ constexpr int kFThreads = 256;
 template <int D> struct FwdTcCfg {
   static constexpr int kTileBytes = tc::kRows * D * 2;         // Q, K or V tile
   static constexpr int kPBytes = tc::kRows * tc::kRows * 2;   // P tile
-  // Q, K x2, V x2, P, half-row maxima/sums, mbarriers + TMEM address, 1 KiB slack
-  static constexpr size_t kSmem = 5 * (size_t)kTileBytes + kPBytes + 2 * tc::kRows * 4 + 64 + 1024;
+  // head_dim 64: the two threads of a row exchange their half-row maxima and
+  // sums through two free tensor-memory columns (192, 193), which keeps two
+  // blocks on an SM; head_dim 128 (one block per SM) uses shared memory
+  static constexpr bool kXchTmem = D == 64;
+  static constexpr int kXchBytes = kXchTmem ? 0 : 2 * tc::kRows * 4;
+  // Q, K x2, V x2, P, exchange, mbarriers + TMEM address (the dynamic shared
+  // memory is 1 KiB aligned: declared so, and checked)
+  static constexpr size_t kSmem = 5 * (size_t)kTileBytes + kPBytes + kXchBytes + 64;
 };
 
 template <typename T, int D>
@@ -294,8 +308,8 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
   constexpr uint32_t kOcol = kRows;           // O accumulator columns [128, 128 + D)
   constexpr int OC = D / 2;                   // O columns per thread
   constexpr float kThresh = 8.f;
-  extern __shared__ __align__(128) unsigned char smem_tc[];
-  unsigned char* smem = smem_tc + ((1024 - (smem_u32(smem_tc) & 1023)) & 1023);
+  extern __shared__ __align__(1024) unsigned char smem_fwd[];
+  unsigned char* smem = smem_fwd;
   const int qt = gridDim.x - 1 - blockIdx.x;  // longest rows first
   const int h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.Hq / p.Hkv);
@@ -309,9 +323,9 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
   const T* vg = (const T*)p.v + ((int64_t)b * p.Hkv + kh) * p.T * D;
   const uint32_t sQ = smem_u32(smem), sK = sQ + FC::kTileBytes, sV = sK + 2 * FC::kTileBytes;
   const uint32_t sP = sV + 2 * FC::kTileBytes;
-  float* xch = reinterpret_cast<float*>(smem + 5 * FC::kTileBytes + FC::kPBytes);  // [2][128]
-  const uint32_t bars = sP + FC::kPBytes + 2 * kRows * 4;  // barS, barPV
-  uint32_t* s_taddr = reinterpret_cast<uint32_t*>(smem + 5 * FC::kTileBytes + FC::kPBytes + 2 * kRows * 4 + 16);
+  float* xch = reinterpret_cast<float*>(smem + 5 * FC::kTileBytes + FC::kPBytes);  // [2][128] (head_dim 128)
+  const uint32_t bars = sP + FC::kPBytes + FC::kXchBytes;  // barS, barPV
+  uint32_t* s_taddr = reinterpret_cast<uint32_t*>(smem + 5 * FC::kTileBytes + FC::kPBytes + FC::kXchBytes + 16);
   const float sl2 = p.scaling * kLog2eP;
   const int n_kt = qt + 1;  // key tiles at or below the diagonal
 
@@ -343,8 +357,6 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
     }
     commit(bars + 8);
   };
-  // the two threads of a row meet at named barrier 1 + quarter (warps w, w + 4)
-  auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;\n" ::"r"(1 + quarter) : "memory"); };
 
   // cp.async groups: {Q, K_0}, {K_1}, {V_0}, then per tile j {K_j+2}, {V_j+1}
   load_tile128<D, kFThreads>(sQ, qg, q0, p.T);
@@ -362,9 +374,28 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
   const uint32_t tmem = *s_taddr;
   const uint32_t trow = tmem + ((uint32_t)(32 * quarter) << 16);  // this warp's lane quarter
   const uint32_t tS = trow + 64 * half, tO = trow + kOcol + OC * half;
+  const uint32_t tX = trow + kOcol + D;  // exchange columns (head_dim 64)
+  // half-row value exchange: publish before a block barrier, read after it
+  auto xch_put = [&](float v) {
+    if constexpr (FC::kXchTmem) {
+      st1(tX + half, __float_as_uint(v));
+      st_wait();
+    } else {
+      xch[half * kRows + rl] = v;
+    }
+  };
+  auto xch_get = [&]() -> float {
+    if constexpr (FC::kXchTmem) {
+      const uint32_t v = ld1(tX + (half ^ 1));
+      ld_wait();
+      return __uint_as_float(v);
+    } else {
+      return xch[(half ^ 1) * kRows + rl];
+    }
+  };
   if (threadIdx.x == 0) issue_s(0, tmem);
 
-  bool lost = false;
+  bool lost = (smem_u32(smem_fwd) & 1023) != 0;  // swizzled tiles need 1 KiB alignment
   float m_run = -INFINITY, m_thr = -INFINITY, l_run = 0.f;
   for (int j = 0; j < n_kt; ++j) {
     const int k0 = j * kRows + 64 * half;           // first key of this thread's columns
@@ -385,7 +416,7 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
       r[i] = __float_as_uint(x);
       mx = fmaxf(mx, x);
     }
-    xch[half * kRows + rl] = mx;
+    xch_put(mx);
     // every thread has read S_j and K_{j+1} is resident: the next QK MMA
     // runs during the rest of this tile
     cp_wait<2>();
@@ -394,7 +425,7 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
     __syncthreads();
     fence_after();
     if (threadIdx.x == 0 && j + 1 < n_kt) issue_s(j + 1, tmem);
-    mx = fmaxf(mx, xch[(half ^ 1) * kRows + rl]);
+    mx = fmaxf(mx, xch_get());
     // PV_{j-1} done: P, V_{j-1} and O are free
     if (j > 0 && !bar_wait(bars + 8, (j - 1) & 1)) lost = true;
     fence_after();
@@ -450,9 +481,11 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
   }
   if (!bar_wait(bars + 8, (n_kt - 1) & 1)) lost = true;
   fence_after();
-  xch[half * kRows + rl] = l_run;
-  pair_sync();
-  const float l_row = l_run + xch[(half ^ 1) * kRows + rl];
+  xch_put(l_run);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const float l_row = l_run + xch_get();
   // O / l into this thread's half of the output row; log-sum-exp
   const float inv = lost ? __int_as_float(0x7fc00000) : 1.f / l_row;
   T* orow = (T*)p.out + (((int64_t)b * p.T + row) * p.Hq + h) * D + OC * half;
@@ -486,6 +519,8 @@ int launch(const PrefillParams& p, bool colmass, cudaStream_t stream) {
   using FC = FwdTcCfg<D>;
   const dim3 grid((p.T + tc::kRows - 1) / tc::kRows, p.Hq, p.B);
   cudaFuncSetAttribute(prefill_fwd_tc_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FC::kSmem);
+  // the whole unified L1 as shared memory, so two head_dim-64 blocks fit an SM
+  cudaFuncSetAttribute(prefill_fwd_tc_kernel<T, D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   prefill_fwd_tc_kernel<T, D><<<grid, kFThreads, FC::kSmem, stream>>>(p);
   SKV_CHECK_LAUNCH();
   if (colmass) {
