@@ -28,7 +28,6 @@ namespace {
 
 using namespace mma;
 
-constexpr int kPThreads = 128;   // threads of the scoring kernel: one key row each
 constexpr float kLog2eP = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
@@ -131,7 +130,7 @@ __device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t addr, uint32_t lbo) {
 
 // 128 rows x D of a [T][D] matrix into K-major 128-byte-swizzled halves of 64
 // channels (rows >= T zero-filled).
-template <int D, int NT = kPThreads>
+template <int D, int NT>
 __device__ __forceinline__ void load_tile128(uint32_t dst, const void* src, int row0, int T) {
   constexpr int CPR = D / 8;                  // 16-byte chunks per row
   constexpr int HALF = kRows * 128;           // bytes of one 64-channel half
@@ -154,8 +153,10 @@ template <int D> struct TcCfg {
 
 }  // namespace tc
 
+constexpr int kCThreads = 256;  // scoring: two threads per key row
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kCThreads) prefill_colmass_tc_kernel(const PrefillParams p) {
   using namespace tc;
   using TC = TcCfg<D>;
   constexpr bool kBF = !std::is_same<T, __half>::value;
@@ -167,6 +168,7 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.Hq / p.Hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3, half = warp >> 2;  // key rows 32*quarter.., query columns 64*half..
   const int k0 = kt * kRows;
   const T* qg = (const T*)p.q + ((int64_t)b * p.Hq + h) * p.T * D;
   const T* kg = (const T*)p.k + ((int64_t)b * p.Hkv + kh) * p.T * D;
@@ -189,9 +191,11 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
   }
   auto load_q = [&](int i) {  // query tile i of this block into buffer i & 1
     const int q0 = k0 + i * kRows, buf = i & 1;
-    load_tile128<D>(sQ + buf * TC::kTileBytes, qg, q0, p.T);
-    const int row = q0 + threadIdx.x;  // kPThreads == kRows
-    sL[buf * kRows + threadIdx.x] = row < p.T ? lse[row] : INFINITY;  // rows past the end weigh 0
+    load_tile128<D, kCThreads>(sQ + buf * TC::kTileBytes, qg, q0, p.T);
+    if (threadIdx.x < kRows) {
+      const int row = q0 + threadIdx.x;
+      sL[buf * kRows + threadIdx.x] = row < p.T ? lse[row] : INFINITY;  // rows past the end weigh 0
+    }
   };
   auto issue = [&](int i, uint32_t tmem) {  // S^T tile i into accumulator buffer i & 1
     const uint32_t qb = sQ + (i & 1) * TC::kTileBytes;
@@ -203,7 +207,7 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
     commit(bars + 8 * (i & 1));
   };
 
-  load_tile128<D>(sK, kg, k0, p.T);
+  load_tile128<D, kCThreads>(sK, kg, k0, p.T);
   load_q(0);
   cp_commit();
   if (n_qt > 1) load_q(1);
@@ -217,8 +221,9 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
   if (threadIdx.x == 0) issue(0, tmem);
 
   bool lost = false;
-  float cs = 0.f;                        // column mass of this thread's key
-  const int key = k0 + 32 * warp + lane;  // accumulator row (tensor-memory lane)
+  float cs = 0.f;                                 // this thread's share of its key's column mass
+  const int rl = 32 * quarter + lane;
+  const int key = k0 + rl;                        // accumulator row (tensor-memory lane)
   for (int i = 0; i < n_qt; ++i) {
     if (i + 1 < n_qt) {  // the next tile's MMA runs while this one is read
       cp_wait<0>();
@@ -230,20 +235,19 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
     }
     if (!bar_wait(bars + 8 * (i & 1), (i >> 1) & 1)) lost = true;
     fence_after();
-    const int q0 = k0 + i * kRows;
-    const float* lt = sL + (i & 1) * kRows;
-    const uint32_t tacc = tmem + ((uint32_t)(32 * warp) << 16) + (i & 1) * kRows;
-#pragma unroll 1
-    for (int c0 = 0; c0 < kRows; c0 += 32) {
-      uint32_t r[32];
-      ld32(r, tacc + c0);
-      ld_wait();
+    const int c0 = 64 * half;
+    const int qa = k0 + i * kRows + c0;           // first query of this thread's columns
+    const float* lt = sL + (i & 1) * kRows + c0;
+    const uint32_t tacc = tmem + ((uint32_t)(32 * quarter) << 16) + (i & 1) * kRows + c0;
+    uint32_t r[64];
+    ld32(*reinterpret_cast<uint32_t(*)[32]>(r), tacc);
+    ld32(*reinterpret_cast<uint32_t(*)[32]>(r + 32), tacc + 32);
+    ld_wait();
+    const bool diag = i == 0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int q = q0 + c0 + j;
-        const float x = ex2(__uint_as_float(r[j]) * sl2 - lt[c0 + j]);
-        cs += (i == 0 && q < key) ? 0.f : x;
-      }
+    for (int j = 0; j < 64; ++j) {
+      const float x = ex2(__uint_as_float(r[j]) * sl2 - lt[j]);
+      cs += (diag && qa + j < key) ? 0.f : x;
     }
     // every thread is done with accumulator i & 1 and query buffer i & 1
     fence_before();
@@ -254,10 +258,13 @@ __global__ void __launch_bounds__(kPThreads) prefill_colmass_tc_kernel(const Pre
     }
     cp_commit();
   }
-  if (key < p.T) p.colmass[((int64_t)b * p.Hq + h) * p.T + key] = lost ? __int_as_float(0x7fc00000) : cs;
+  // the two halves of each key's column mass (sL is free now)
+  if (half == 1) sL[rl] = cs;
   fence_before();
   __syncthreads();
   fence_after();
+  if (half == 0 && key < p.T)
+    p.colmass[((int64_t)b * p.Hq + h) * p.T + key] = lost ? __int_as_float(0x7fc00000) : cs + sL[rl];
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem));
 }
 
@@ -528,7 +535,7 @@ int launch(const PrefillParams& p, bool colmass, cudaStream_t stream) {
     cudaFuncSetAttribute(prefill_colmass_tc_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)TC::kSmem);
     const dim3 g2((p.T + tc::kRows - 1) / tc::kRows, p.Hq, p.B);
-    prefill_colmass_tc_kernel<T, D><<<g2, kPThreads, TC::kSmem, stream>>>(p);
+    prefill_colmass_tc_kernel<T, D><<<g2, kCThreads, TC::kSmem, stream>>>(p);
     SKV_CHECK_LAUNCH();
   }
   return SKV_OK;
