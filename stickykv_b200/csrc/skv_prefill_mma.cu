@@ -243,11 +243,15 @@ __global__ void __launch_bounds__(kCThreads) prefill_colmass_tc_kernel(const Pre
     ld32(*reinterpret_cast<uint32_t(*)[32]>(r), tacc);
     ld32(*reinterpret_cast<uint32_t(*)[32]>(r + 32), tacc + 32);
     ld_wait();
-    const bool diag = i == 0;
+    if (i == 0) {  // diagonal tile: queries before the key do not see it
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const float x = ex2(__uint_as_float(r[j]) * sl2 - lt[j]);
-      cs += (diag && qa + j < key) ? 0.f : x;
+      for (int j = 0; j < 64; ++j) {
+        const float x = ex2(fmaf(__uint_as_float(r[j]), sl2, -lt[j]));
+        cs += qa + j < key ? 0.f : x;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) cs += ex2(fmaf(__uint_as_float(r[j]), sl2, -lt[j]));
     }
     // every thread is done with accumulator i & 1 and query buffer i & 1
     fence_before();
@@ -415,14 +419,21 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
     if (j + 2 < n_kt) load_tile128<D, kFThreads>(sK + (j & 1) * FC::kTileBytes, kg, (j + 2) * kRows, p.T);
     cp_commit();
     ld_wait();
+    // row max of the raw scores (scaling is monotone); keys past the causal
+    // diagonal or the prompt become -inf, so they exponentiate to 0 below
     float mx = -INFINITY;
+    if (edge) {
+      const int lim = min(row + 1, p.T) - k0;  // keys k0 + i with i < lim are valid
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      float x = __uint_as_float(r[i]) * sl2;
-      if (edge && (k0 + i > row || k0 + i >= p.T)) x = -INFINITY;
-      r[i] = __float_as_uint(x);
-      mx = fmaxf(mx, x);
+      for (int i = 0; i < 64; ++i) {
+        if (i >= lim) r[i] = __float_as_uint(-INFINITY);
+        mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
     }
+    mx *= sl2;
     xch_put(mx);
     // every thread has read S_j and K_{j+1} is resident: the next QK MMA
     // runs during the rest of this tile
@@ -467,8 +478,8 @@ __global__ void __launch_bounds__(kFThreads, D == 64 ? 2 : 1) prefill_fwd_tc_ker
       uint32_t pk[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float x0 = ex2(__uint_as_float(r[8 * c + 2 * e]) - m_run);
-        const float x1 = ex2(__uint_as_float(r[8 * c + 2 * e + 1]) - m_run);
+        const float x0 = ex2(fmaf(__uint_as_float(r[8 * c + 2 * e]), sl2, -m_run));
+        const float x1 = ex2(fmaf(__uint_as_float(r[8 * c + 2 * e + 1]), sl2, -m_run));
         rs += x0 + x1;
         pk[e] = O::pack(x0, x1);
       }
