@@ -281,7 +281,8 @@ def test_prefill_scores_match_reference_golden():
 
 
 @pytest.mark.parametrize("dt,D,G,T", [("f16", 64, 4, 333), ("bf16", 64, 4, 333), ("bf16", 128, 2, 700),
-                                       ("f16", 128, 8, 129), ("f16", 64, 1, 64)])
+                                       ("f16", 128, 8, 129), ("f16", 64, 1, 64), ("bf16", 64, 4, 1),
+                                       ("f16", 64, 2, 256), ("bf16", 128, 4, 1100)])
 def test_prefill_matches_oracle(dt, D, G, T):
     """Tensor-core prefill (fp16/bf16, head_dim 64/128): output against torch
     fp32 attention, prompt window scores against the oracle; partial last
