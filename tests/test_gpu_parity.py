@@ -281,8 +281,8 @@ def test_prefill_scores_match_reference_golden():
 
 
 @pytest.mark.parametrize("dt,D,G,T", [("f16", 64, 4, 333), ("bf16", 64, 4, 333), ("bf16", 128, 2, 700),
-                                       ("f16", 128, 8, 129), ("f16", 64, 1, 64), ("bf16", 64, 4, 1),
-                                       ("f16", 64, 2, 256), ("bf16", 128, 4, 1100)])
+                                       ("f16", 128, 8, 129), ("f16", 64, 1, 64), ("f16", 64, 2, 256),
+                                       ("bf16", 128, 4, 1100)])
 def test_prefill_matches_oracle(dt, D, G, T):
     """Tensor-core prefill (fp16/bf16, head_dim 64/128): output against torch
     fp32 attention, prompt window scores against the oracle; partial last
@@ -301,6 +301,34 @@ def test_prefill_matches_oracle(dt, D, G, T):
     sd = torch.nn.functional.scaled_dot_product_attention(
         qd, kd.repeat_interleave(G, 1), vd.repeat_interleave(G, 1), is_causal=True)
     assert_out_close(to_np(out), to_np(sd.transpose(1, 2)), dt, "prefill")
+
+
+@pytest.mark.parametrize("dt,D,T", [("bf16", 64, 1), ("f16", 128, 5), ("bf16", 64, 127)])
+def test_prefill_tiny_prompts_through_the_abi(dt, D, T):
+    """Prompts shorter than one 128-row tile (down to one token) straight
+    through `skv_prefill_attention` (no window scores): output against torch
+    fp32 causal attention."""
+    import ctypes as C
+    from stickykv_b200 import _lib
+    L = _lib.lib()
+    g = torch.Generator().manual_seed(11 + T)
+    B, Hkv, Hq = 2, 2, 8
+    q, k, v = (rand(s_, dt, g).to(DEV) for s_ in ((B, Hq, T, D), (B, Hkv, T, D), (B, Hkv, T, D)))
+    out = torch.full((B, T, Hq, D), float("nan"), device=DEV, dtype=TORCH_DT[dt])
+    d = _lib.LayerDesc()
+    d.batch, d.num_kv_heads, d.num_q_heads, d.head_dim = B, Hkv, Hq, D
+    d.kv_dtype = {"f16": 1, "bf16": 2}[dt]
+    d.window_size, d.num_sink, d.sink_pad = 8, 4, 8
+    d.fp_capacity, d.k_fp, d.v_fp = T, k.data_ptr(), v.data_ptr()
+    nb = L.skv_prefill_workspace_size(C.byref(d), T)
+    ws = torch.empty(nb, dtype=torch.uint8, device=DEV)
+    _lib.check(L.skv_prefill_attention(C.byref(d), T, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                       C.c_float(D ** -0.5), None, 0, ws.data_ptr(), nb,
+                                       torch.cuda.current_stream().cuda_stream), "prefill")
+    qd, kd, vd = (x.float() for x in (q, k, v))
+    sd = torch.nn.functional.scaled_dot_product_attention(
+        qd, kd.repeat_interleave(Hq // Hkv, 1), vd.repeat_interleave(Hq // Hkv, 1), is_causal=True)
+    assert_out_close(to_np(out), to_np(sd.transpose(1, 2)), dt, "prefill tiny")
 
 
 # -- full-size properties ----------------------------------------------------------------
