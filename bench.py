@@ -333,7 +333,10 @@ def run_e2e(args, rank, world, dev):
     greedily decodes 256 tokens with the windowed cache (budget 0.40, int4
     tier).  The global batch of 32 rows is split across the ranks; decode
     tokens/s = rows x steps / decode time (max over ranks), prefill excluded.
-    At N > 1 the ranks all-gather each step's greedy tokens."""
+    At N > 1 the ranks all-gather each step's greedy tokens.  Also reported,
+    as the reference's perf runner does: time to first token (the prefill
+    forward), time per output token and peak device memory; `--e2e-budget`
+    sets the cache budget (0.10 / 0.25 / 0.50 in the reference's sweep)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -346,6 +349,7 @@ def run_e2e(args, rank, world, dev):
         c["prompt"] = args.e2e_prompt
     if args.e2e_decode:
         c["decode"] = args.e2e_decode
+    budget = args.e2e_budget or BUDGET
     rows = max(1, c["batch"] // world)
     cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["ffn"],
                       num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
@@ -355,7 +359,8 @@ def run_e2e(args, rank, world, dev):
     with torch.device(dev):
         model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
     wcfg = WindowedCacheConfig(window_size=WS, num_sink_tokens=SINKS, local_window_size=LOCAL,
-                               cache_budget=BUDGET, int4_tier=True)
+                               cache_budget=budget, int4_tier=True)
+    torch.cuda.reset_peak_memory_stats(dev)
     cache = WindowedCache(wcfg, c["prompt"], model.config, torch.bfloat16, model.model.rotary_emb,
                           num_layers=c["layers"], max_tokens=c["decode"])
     handles = install_score_hooks(model, cache, wcfg)
@@ -390,10 +395,11 @@ def run_e2e(args, rank, world, dev):
             dist.barrier()
         clocks = sampler.stop()
     handles.remove()
-    t = torch.tensor([t0.elapsed_time(t1), p0.elapsed_time(p1)], device=dev, dtype=torch.float64)
+    t = torch.tensor([t0.elapsed_time(t1), p0.elapsed_time(p1), torch.cuda.max_memory_allocated(dev)],
+                     device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dec_ms, pre_ms = (float(x) for x in t.tolist())
+    dec_ms, pre_ms, peak = (float(x) for x in t.tolist())
     if rank != 0:
         return None
     steps = c["decode"] - 1
@@ -407,9 +413,10 @@ def run_e2e(args, rank, world, dev):
                                "windowed cache", "layers": c["layers"], "hidden": c["hidden"],
                    "q_heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
                    "global_batch": total_rows, "prompt": c["prompt"], "decode_steps": c["decode"],
-                   "cache_budget": BUDGET, "retained_tokens": cache.get_seq_length(0),
+                   "cache_budget": budget, "retained_tokens": cache.get_seq_length(0),
                    "parallelism": f"{world} batch shards"},
-        "prefill_ms": pre_ms, "clocks": clocks,
+        "prefill_ms": pre_ms, "ttft_ms": pre_ms, "tpot_ms": dec_ms / steps,
+        "peak_mem_gib": peak / 2 ** 30, "clocks": clocks,
     }
 
 
@@ -571,6 +578,7 @@ def main():
                     help="end-to-end decode through a Llama-3.2-1B-shaped transformers model instead")
     ap.add_argument("--e2e-prompt", type=int, default=0)
     ap.add_argument("--e2e-decode", type=int, default=0)
+    ap.add_argument("--e2e-budget", type=float, default=0.0)
     ap.add_argument("--no-tier", action="store_true",
                     help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
     ap.add_argument("--tile-profile", action="store_true",
