@@ -89,6 +89,31 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
 
 
+def max_over_ranks(values, dev, world):
+    """Element-wise max of per-rank timings over all ranks (every rank gets
+    the result; the job is as slow as its slowest rank)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def rows_per_rank(batch, world):
+    """Rows of a global batch each rank decodes (batch shards; no row is shared)."""
+    return max(1, batch // world)
+
+
+def gather_tokens(nxt, gathered, world):
+    """All-gather every rank's next tokens [rows, 1] into `gathered`
+    [world * rows, 1] in rank order (the end-to-end run's one collective)."""
+    import torch.distributed as dist
+    if world > 1:
+        dist.all_gather_into_tensor(gathered, nxt)
+    return gathered if world > 1 else nxt
+
+
 def build_steady_cache(dev, seed, tier=True):
     """A layer cache at 32k context after its first eviction (steady state)."""
     import numpy as np
@@ -234,11 +259,7 @@ def run_ours(args, rank, world, dev):
     e2e_ms = e0.elapsed_time(e1)
     h2d = din.numel() * 2
     d2h = hout[0].numel() * 2
-    # max over ranks
-    t = torch.tensor([ms, e2e_ms, float(np.mean(attn_ms))], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, attn_avg = (float(x) for x in t.tolist())
+    ms, e2e_ms, attn_avg = max_over_ranks([ms, e2e_ms, float(np.mean(attn_ms))], dev, world)
     if rank != 0:
         return None
     peak, peak_kind = measured_hbm_peak()
@@ -350,7 +371,7 @@ def run_e2e(args, rank, world, dev):
     if args.e2e_decode:
         c["decode"] = args.e2e_decode
     budget = args.e2e_budget or BUDGET
-    rows = max(1, c["batch"] // world)
+    rows = rows_per_rank(c["batch"], world)
     cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["ffn"],
                       num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
                       num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], rope_theta=c["theta"],
@@ -388,18 +409,15 @@ def run_e2e(args, rank, world, dev):
             out = model(input_ids=nxt, past_key_values=cache, use_cache=True, logits_to_keep=1)
             nxt = out.logits[:, -1].argmax(-1, keepdim=True)
             if gathered is not None:
-                dist.all_gather_into_tensor(gathered, nxt)
+                gather_tokens(nxt, gathered, world)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         clocks = sampler.stop()
     handles.remove()
-    t = torch.tensor([t0.elapsed_time(t1), p0.elapsed_time(p1), torch.cuda.max_memory_allocated(dev)],
-                     device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dec_ms, pre_ms, peak = (float(x) for x in t.tolist())
+    dec_ms, pre_ms, peak = max_over_ranks(
+        [t0.elapsed_time(t1), p0.elapsed_time(p1), torch.cuda.max_memory_allocated(dev)], dev, world)
     if rank != 0:
         return None
     steps = c["decode"] - 1
