@@ -1,5 +1,5 @@
 // Tensor-core decode attention with fused window mass (fp16/bf16 KV,
-// window_size 8, 4 query heads per KV head, head_dim 64 or 128).
+// window_size 8, 1, 2, 4 or 8 query heads per KV head, head_dim 64 or 128).
 //
 // Same contract as the portable path (skv_decode_generic.cu): replaces the
 // reference's attention + score hook + scorer for one decode query
@@ -11,7 +11,11 @@
 // window_size 8 every unit after the sinks is one scoring window.  A tile is
 // two consecutive units (16 tokens).
 //
-// Work split: one CTA per (row, kv head, unit range); ranges are balanced by
+// Query heads are handled in groups of four MMA columns: GQA 4 is one group
+// per kv head, GQA 8 two (each reads the kv head's cache once), GQA 1 and 2 one
+// group whose spare columns carry a zero query and are never stored.
+//
+// Work split: one CTA per (row, head group, unit range); ranges are balanced by
 // an estimated per-tile cost.  Each of the 4 warps takes a contiguous run of
 // the CTA's tiles (again cost-balanced) and streams it through a private
 // cp.async ring in shared memory, so the main loop has no CTA barrier.  A
@@ -83,13 +87,18 @@ struct MmaParams {
   const void* q;
   void* out;
   float* scores;   // [B][Hq][scores_cap] accumulator (may be null)
-  float* part;     // [B][Hkv][n_split][4][D+2]: O, max (log2 domain), sum
-  float* mass;     // [B][Hq][W]: window mass relative to its split's max
+  float* part;     // [B][Hv][n_split][4][D+2]: O, max (log2 domain), sum
+  float* mass;     // [B][Hv][4][W]: window mass relative to its split's max
   const void* k_new;  // optional token appended by the last split's blocks
   const void* v_new;
   int64_t q_sb, q_sh, o_sb, o_sh, kn_sb, kn_sh;
   int new_slot;       // fp slot of the appended token
   int B, Hkv, cap, page_cap, scores_cap, n_split;
+  // query-head groups: the kernel works on Hv groups of 4 query heads.  GQA 8
+  // splits each kv head into rep = 2 groups (its K/V read once per group);
+  // GQA 1 and 2 give each kv head one group of G4 = G heads, the remaining
+  // columns carry a zero query and are never stored.
+  int Hq, Hv, rep, G4;
   int s, s_eff, s_pad, NS, n_tp, rest, U, W, rope_rows;
   float scale_log2;
   int bnd[kMaxSplits + 1];
@@ -204,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   constexpr int I4_IT = (2 * PG_CH + 31) / 32;            // chunks per lane for a page pair
   constexpr float kThresh = 8.f;                          // lazy rescale margin (log2 domain)
   extern __shared__ __align__(128) unsigned char smem[];
-  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;  // kh: query-head group
+  const int kr = kh / p.rep;                                       // its kv head
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int u0 = p.bnd[split], u1 = p.bnd[split + 1];
@@ -222,10 +232,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
     // value rows before any copy of this block reads them (the barrier below
     // orders the stores before the cp.async reads)
     constexpr int VPR = D / 8;  // 16-byte vectors per row
-    const int64_t row = (((int64_t)b * p.Hkv + kh) * p.cap + p.new_slot) * D;
+    const int64_t row = (((int64_t)b * p.Hkv + kr) * p.cap + p.new_slot) * D;
     for (int e = threadIdx.x; e < 2 * VPR; e += kThreads) {
       const int which = e / VPR, c = e - which * VPR;
-      const T* src = (const T*)(which ? p.v_new : p.k_new) + b * p.kn_sb + kh * p.kn_sh + c * 8;
+      const T* src = (const T*)(which ? p.v_new : p.k_new) + b * p.kn_sb + kr * p.kn_sh + c * 8;
       T* dst = (T*)(which ? p.v_fp : p.k_fp) + row + c * 8;
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
     }
@@ -251,8 +261,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   const int te = warp == kWarps - 1 ? n_tiles : tr.at_cost((total * (warp + 1) + kWarps - 1) / kWarps);
   __syncthreads();
 
-  const int64_t kv_row = ((int64_t)b * p.Hkv + kh) * p.cap * D;
-  const int64_t pg_row = ((int64_t)b * p.Hkv + kh) * p.page_cap;
+  const int64_t kv_row = ((int64_t)b * p.Hkv + kr) * p.cap * D;
+  const int64_t pg_row = ((int64_t)b * p.Hkv + kr) * p.page_cap;
   const T* kfp = (const T*)p.k_fp + kv_row;
   const T* vfp = (const T*)p.v_fp + kv_row;
   const unsigned char* pages_l = p.pages + pg_row * PB + lane * 16;
@@ -264,7 +274,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   const uint32_t vs_off = page_v_scales_off(D) + t * NW * 8;
 
   // query of head (g & 3) in B-fragment order: d = 16kb + 2t + {0,1,8,9}
-  const T* qp = (const T*)p.q + b * p.q_sb + (kh * 4 + (g & 3)) * p.q_sh;
+  const bool q_live = (g & 3) < p.G4;  // columns past the group's heads carry a zero query
+  const T* qp = (const T*)p.q + b * p.q_sb + (kh * p.G4 + (q_live ? (g & 3) : 0)) * p.q_sh;
+  const float q_scl = q_live ? 1.f : 0.f;
+  const uint32_t q_bits = q_live ? 0xFFFFFFFFu : 0u;
   // query rotated to the page start of this thread's column (int4 columns)
   float rq[KB][4];
   int rq_pos = -1;
@@ -277,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       for (int e = 0; e < 4; ++e) {
         const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
         const float c = p.cos[(int64_t)P * (D / 2) + d], s = p.sin[(int64_t)P * (D / 2) + d];
-        const float x = ld_f32(qp + d), y = ld_f32(qp + d + D / 2);
+        const float x = q_live ? ld_f32(qp + d) : 0.f, y = q_live ? ld_f32(qp + d + D / 2) : 0.f;
         rq[kb][e] = fmaf(x, c, y * s) * scl;
         rq[kb + KB / 2][e] = fmaf(y, c, -x * s) * scl;
       }
@@ -285,8 +298,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   auto load_qb = [&](uint32_t (&qb)[KB][2]) {
 #pragma unroll
     for (int kb = 0; kb < KB; ++kb) {
-      qb[kb][0] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t);
-      qb[kb][1] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t + 8);
+      qb[kb][0] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t) & q_bits;
+      qb[kb][1] = *reinterpret_cast<const uint32_t*>(qp + 16 * kb + 2 * t + 8) & q_bits;
     }
   };
 
@@ -724,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
         acc += ex2(mw - M) * (c == D + 1 ? wl[w * 4 + hh] : wo[(w * 4 + hh) * D + c]);
       }
     }
-    p.part[(((int64_t)b * p.Hkv + kh) * p.n_split + split) * 4 * (D + 2) + e] = acc;
+    p.part[(((int64_t)b * p.Hv + kh) * p.n_split + split) * 4 * (D + 2) + e] = acc;
   }
   const int n_units = u1 - u0;
   {
@@ -736,12 +749,12 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       const int i = k >> 1, h = k & 1;
       const float mt = mass_s[i * 12 + 8 + hh];
       const float val = (mt == -INFINITY) ? 0.f : mass_s[i * 12 + h * 4 + hh] * ex2(mt - s_M[hh]);
-      p.mass[((int64_t)b * p.Hkv * 4 + kh * 4 + hh) * p.W + (u - R.NS)] = val;
+      p.mass[((int64_t)b * p.Hv * 4 + kh * 4 + hh) * p.W + (u - R.NS)] = val;
     }
   }
 }
 
-// Combine the splits of one (row, kv head) for its 4 query heads: the block
+// Combine the splits of one (row, head group) for its query heads: the block
 // with blockIdx.x == 0 writes the output, every block adds the normalised
 // mass of its window chunk.  It is launched as a programmatic dependent of
 // the decode kernel: its blocks start while the decode's last blocks run,
@@ -753,25 +766,24 @@ constexpr int kMergeWindows = kMergePer * kMergeThreads;   // windows per block
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const __grid_constant__ MmaParams p) {
-  const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-  const int Hq = p.Hkv * 4;
+  const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;  // kh: query-head group
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float s_f[4][kMaxSplits];   // split factor / L per head
   __shared__ int s_bnd[kMaxSplits + 1];
   const int w0 = chunk * kMergeWindows, w_end = min(p.W, w0 + kMergeWindows);
-  float* acc = p.scores ? p.scores + ((int64_t)b * Hq + kh * 4) * p.scores_cap : nullptr;
+  float* acc = p.scores ? p.scores + ((int64_t)b * p.Hq + kh * p.G4) * p.scores_cap : nullptr;
   float av[4][kMergePer];
 #pragma unroll
   for (int hh = 0; hh < 4; ++hh)
 #pragma unroll
     for (int k = 0; k < kMergePer; ++k) {
       const int w = w0 + threadIdx.x + k * kMergeThreads;
-      av[hh][k] = (acc && w < w_end) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
+      av[hh][k] = (acc && w < w_end && hh < p.G4) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
     }
   for (int j = threadIdx.x; j <= p.n_split; j += kMergeThreads) s_bnd[j] = p.bnd[j];
   grid_dependency_wait();
-  const float* part = p.part + ((int64_t)b * p.Hkv + kh) * p.n_split * 4 * (D + 2);
-  const float* ms = p.mass + ((int64_t)b * Hq + kh * 4) * p.W;
+  const float* part = p.part + ((int64_t)b * p.Hv + kh) * p.n_split * 4 * (D + 2);
+  const float* ms = p.mass + ((int64_t)b * p.Hv * 4 + kh * 4) * p.W;
   float mv[4][kMergePer];
 #pragma unroll
   for (int hh = 0; hh < 4; ++hh)
@@ -823,7 +835,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       for (int sp = 0; sp < kPre; ++sp) o += s_f[hh][sp < p.n_split ? sp : 0] * ov[q][sp];
 #pragma unroll 8
       for (int sp = kPre; sp < p.n_split; ++sp) o += s_f[hh][sp] * part[(sp * 4 + hh) * (D + 2) + c];
-      st_f32((T*)p.out + b * p.o_sb + (kh * 4 + hh) * p.o_sh + c, o);
+      if (hh < p.G4) st_f32((T*)p.out + b * p.o_sb + (kh * p.G4 + hh) * p.o_sh + c, o);
     }
   }
   if (acc == nullptr) return;
@@ -838,7 +850,8 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       if (s_bnd[mid] <= u) lo = mid; else hi = mid - 1;
     }
 #pragma unroll
-    for (int hh = 0; hh < 4; ++hh) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
+    for (int hh = 0; hh < 4; ++hh)
+      if (hh < p.G4) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
   }
 }
 
@@ -853,7 +866,7 @@ void plan_splits(MmaParams& p) {
     return (int64_t)kCostGeneric * clampi(u, 0, p.NS) + (int64_t)kCostI4 * clampi(u - p.NS, 0, p.n_tp) +
            (int64_t)kCostFp * clampi(u - TB, 0, UF - TB) + (int64_t)kCostGeneric * max(0, u - UF);
   };
-  const int units = p.B * p.Hkv;
+  const int units = p.B * p.Hv;
   const int slots = 148 * (D == 64 ? 4 : 2);
   int n = max(1, (2 * slots) / max(1, units));
   n = max(n, ceil_div(p.U, kMaxUnitsPerSplit));
@@ -889,10 +902,10 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
   using C = Cfg<D>;
   static_assert(C::kSmemBytes <= 227 * 1024, "smem");
   cudaFuncSetAttribute(decode_mma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmemBytes);
-  decode_mma_kernel<T, D><<<dim3(p.n_split, p.Hkv, p.B), kThreads, C::kSmemBytes, stream>>>(p);
+  decode_mma_kernel<T, D><<<dim3(p.n_split, p.Hv, p.B), kThreads, C::kSmemBytes, stream>>>(p);
   SKV_CHECK_LAUNCH();
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(p.scores ? max(1, ceil_div(p.W, kMergeWindows)) : 1, p.Hkv, p.B);
+  cfg.gridDim = dim3(p.scores ? max(1, ceil_div(p.W, kMergeWindows)) : 1, p.Hv, p.B);
   cfg.blockDim = dim3(kMergeThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
@@ -912,11 +925,17 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
 struct MmaWs {
   size_t part, mass, total;
 };
+// query-head groups of 4 columns: GQA 8 gives two per kv head, GQA 1/2/4 one
+int head_groups(const skv_layer_desc* L) {
+  return L->num_kv_heads * (L->num_q_heads > 4 * L->num_kv_heads ? L->num_q_heads / (4 * L->num_kv_heads) : 1);
+}
+
 MmaWs mma_ws(const skv_layer_desc* L, int T) {
   MmaWs w{};
   const int W = T > L->num_sink ? (T - L->num_sink + L->window_size - 1) / L->window_size : 0;
-  w.part = align_up((size_t)L->batch * L->num_kv_heads * kMaxSplits * 4 * (L->head_dim + 2) * 4, 256);
-  w.mass = align_up((size_t)L->batch * L->num_q_heads * (W > 0 ? W : 1) * 4, 256);
+  const int Hv = head_groups(L);
+  w.part = align_up((size_t)L->batch * Hv * kMaxSplits * 4 * (L->head_dim + 2) * 4, 256);
+  w.mass = align_up((size_t)L->batch * Hv * 4 * (W > 0 ? W : 1) * 4, 256);
   w.total = w.part + w.mass;
   return w;
 }
@@ -924,8 +943,10 @@ MmaWs mma_ws(const skv_layer_desc* L, int T) {
 }  // namespace
 
 bool decode_mma_supported(const skv_layer_desc* L) {
+  const int G = L->num_q_heads / L->num_kv_heads;
   return (L->kv_dtype == SKV_F16 || L->kv_dtype == SKV_BF16) && (L->head_dim == 64 || L->head_dim == 128) &&
-         L->num_q_heads == 4 * L->num_kv_heads && L->window_size == kPageTokens && L->fp_capacity % 8 == 0;
+         (G == 1 || G == 2 || G == 4 || G == 8) && L->num_q_heads == G * L->num_kv_heads &&
+         L->window_size == kPageTokens && L->fp_capacity % 8 == 0;
 }
 
 // Lengths the split plan covers: at least one full tile, at most
@@ -954,6 +975,10 @@ int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, in
   p.mass = (float*)((char*)ws + w.part);
   p.q_sb = q_sb; p.q_sh = q_sh; p.o_sb = o_sb; p.o_sh = o_sh;
   p.B = L->batch; p.Hkv = L->num_kv_heads; p.cap = L->fp_capacity; p.page_cap = L->tier_page_capacity;
+  p.Hq = L->num_q_heads;
+  p.Hv = head_groups(L);
+  p.rep = p.Hv / p.Hkv;
+  p.G4 = p.Hq / p.Hv;
   p.scores_cap = scores_cap;
   p.s = L->num_sink; p.s_pad = L->sink_pad; p.n_tp = tier_pages;
   p.s_eff = T < p.s ? T : p.s;

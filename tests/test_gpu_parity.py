@@ -99,7 +99,8 @@ def test_decode_matches_reference_eager_golden(dt):
 
 
 @pytest.mark.parametrize("dt,D,G,S", [("f32", 64, 2, 300), ("f16", 64, 4, 1000), ("bf16", 128, 4, 777),
-                                      ("f16", 128, 8, 64), ("bf16", 64, 1, 2049), ("f16", 32, 4, 5000)])
+                                      ("f16", 128, 8, 64), ("bf16", 64, 1, 2049), ("f16", 32, 4, 5000),
+                                      ("f16", 64, 2, 1500), ("bf16", 64, 8, 3001), ("f16", 128, 1, 900)])
 def test_decode_matches_oracle(dt, D, G, S):
     g = torch.Generator().manual_seed(S + D)
     B, Hkv = 3, 2
@@ -204,9 +205,9 @@ def _drive_pair(dt, tier, B=3, Hkv=2, G=4, D=64, P=203, steps=30, seed=0, budget
     assert evictions == (steps - 1) // 8
 
 
-@pytest.mark.parametrize("dt", ["f32", "bf16", "f16"])
-def test_reference_mode_eviction_bit_exact(dt):
-    for kind, *rest in _drive_pair(dt, tier=False):
+@pytest.mark.parametrize("dt,G", [("f32", 4), ("bf16", 4), ("f16", 4), ("f16", 8), ("bf16", 2)])
+def test_reference_mode_eviction_bit_exact(dt, G):
+    for kind, *rest in _drive_pair(dt, tier=False, G=G):
         if kind == "evict":
             cache, oc = rest
             st = cache._states[0]
@@ -219,10 +220,13 @@ def test_reference_mode_eviction_bit_exact(dt):
             assert_out_close(to_np(out[:, 0]), ref_out, dt, f"step {t}")
 
 
-@pytest.mark.parametrize("dt", ["f16", "bf16"])
-def test_int4_tier_eviction_and_decode(dt):
+@pytest.mark.parametrize("dt,G", [("f16", 4), ("bf16", 4), ("f16", 8), ("bf16", 2), ("f16", 1)])
+def test_int4_tier_eviction_and_decode(dt, G):
+    """int4 tier, every GQA ratio the tensor-core decode takes (head groups
+    of four columns: one per kv head, two at GQA 8, spare columns at GQA 1
+    and 2)."""
     n_checked = 0
-    for kind, *rest in _drive_pair(dt, tier=True, P=403, steps=34, seed=3):
+    for kind, *rest in _drive_pair(dt, tier=True, G=G, P=403, steps=34, seed=3):
         if kind == "evict":
             cache, oc = rest
             st = cache._states[0]
@@ -248,9 +252,7 @@ def test_int4_tier_eviction_and_decode(dt):
 @pytest.mark.parametrize("P", [5000, 6000])
 def test_int4_tier_decode_long_single_head(P):
     """One (row, kv head) with thousands of retained tokens: the decode splits
-    into up to 16 ranges merged inside one thread-block cluster (P=5000 after
-    its eviction) or into more ranges merged by a second kernel (every step
-    before the eviction, and P=6000 after it)."""
+    them into many cost-balanced ranges that a second kernel merges."""
     n = 0
     for kind, *rest in _drive_pair("f16", tier=True, B=1, Hkv=1, P=P, steps=10, seed=P):
         if kind == "decode":
@@ -371,11 +373,12 @@ def test_cfg3_scale_eviction_selection_and_codes():
 
 
 @pytest.mark.parametrize("dt,D,G,tier", [("f16", 64, 4, True), ("bf16", 128, 4, False),
-                                         ("bf16", 64, 4, True), ("f32", 64, 2, False)])
+                                         ("bf16", 64, 4, True), ("f32", 64, 2, False), ("f16", 64, 8, True),
+                                         ("bf16", 128, 2, False)])
 def test_fused_append_decode_matches_append_then_decode(dt, D, G, tier):
     """skv_decode_attention_append == skv_append + skv_decode_attention, bit
     for bit: output, window scores and the fp store (tensor-core path for the
-    fp16/bf16 GQA-4 cases, the portable path for fp32 GQA-2)."""
+    fp16/bf16 cases, the portable path for fp32)."""
     import ctypes as Ct
     from stickykv_b200 import _lib
     L = _lib.lib()
