@@ -1,5 +1,6 @@
 // Tensor-core decode attention with fused window mass (fp16/bf16 KV,
-// window_size 8, 1, 2, 4 or 8 query heads per KV head, head_dim 64 or 128).
+// window_size a multiple of 8, 1, 2, 4 or 8 query heads per KV head,
+// head_dim 64 or 128).
 //
 // Same contract as the portable path (skv_decode_generic.cu): replaces the
 // reference's attention + score hook + scorer for one decode query
@@ -7,9 +8,10 @@
 // hooks.py:199-290, scorer.py:17-109).
 //
 // The retained cache of one (row, kv head) is a sequence of 8-token units:
-// [sink unit(s) | int4 tier pages | fp units after the tier].  With
-// window_size 8 every unit after the sinks is one scoring window.  A tile is
-// two consecutive units (16 tokens).
+// [sink unit(s) | int4 tier pages | fp units after the tier].  A scoring
+// window is window_size / 8 consecutive units after the sinks (one unit at
+// window_size 8): the kernel records the mass of every unit, the merge sums
+// a window's units.  A tile is two consecutive units (16 tokens).
 //
 // Query heads are handled in groups of four MMA columns: GQA 4 is one group
 // per kv head, GQA 8 two (each reads the kv head's cache once), GQA 1 and 2 one
@@ -88,7 +90,7 @@ struct MmaParams {
   void* out;
   float* scores;   // [B][Hq][scores_cap] accumulator (may be null)
   float* part;     // [B][Hv][n_split][4][D+2]: O, max (log2 domain), sum
-  float* mass;     // [B][Hv][4][W]: window mass relative to its split's max
+  float* mass;     // [B][Hv][4][W]: unit mass relative to its split's max
   const void* k_new;  // optional token appended by the last split's blocks
   const void* v_new;
   int64_t q_sb, q_sh, o_sb, o_sh, kn_sb, kn_sh;
@@ -100,6 +102,7 @@ struct MmaParams {
   // columns carry a zero query and are never stored.
   int Hq, Hv, rep, G4;
   int s, s_eff, s_pad, NS, n_tp, rest, U, W, rope_rows;
+  int upw, Ww;  // 8-token units per window (window_size / 8) and windows; W counts units
   float scale_log2;
   int bnd[kMaxSplits + 1];
 };
@@ -276,7 +279,6 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   // query of head (g & 3) in B-fragment order: d = 16kb + 2t + {0,1,8,9}
   const bool q_live = (g & 3) < p.G4;  // columns past the group's heads carry a zero query
   const T* qp = (const T*)p.q + b * p.q_sb + (kh * p.G4 + (q_live ? (g & 3) : 0)) * p.q_sh;
-  const float q_scl = q_live ? 1.f : 0.f;
   const uint32_t q_bits = q_live ? 0xFFFFFFFFu : 0u;
   // query rotated to the page start of this thread's column (int4 columns)
   float rq[KB][4];
@@ -770,7 +772,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float s_f[4][kMaxSplits];   // split factor / L per head
   __shared__ int s_bnd[kMaxSplits + 1];
-  const int w0 = chunk * kMergeWindows, w_end = min(p.W, w0 + kMergeWindows);
+  const int w0 = chunk * kMergeWindows, w_end = min(p.Ww, w0 + kMergeWindows);
   float* acc = p.scores ? p.scores + ((int64_t)b * p.Hq + kh * p.G4) * p.scores_cap : nullptr;
   float av[4][kMergePer];
 #pragma unroll
@@ -790,7 +792,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
 #pragma unroll
     for (int k = 0; k < kMergePer; ++k) {
       const int w = w0 + threadIdx.x + k * kMergeThreads;
-      mv[hh][k] = (acc && w < w_end) ? ms[(int64_t)hh * p.W + w] : 0.f;
+      mv[hh][k] = (acc && w < w_end && p.upw == 1) ? ms[(int64_t)hh * p.W + w] : 0.f;
     }
   // output partials of the first splits, loaded before the statistics exist
   constexpr int kOut = 4 * D / kMergeThreads;  // (head, channel) pairs per thread
@@ -843,15 +845,30 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
   for (int k = 0; k < kMergePer; ++k) {
     const int w = w0 + threadIdx.x + k * kMergeThreads;
     if (w >= w_end) continue;
-    const int u = p.NS + w;
-    int lo = 0, hi = p.n_split - 1;  // last split with bnd <= u
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (s_bnd[mid] <= u) lo = mid; else hi = mid - 1;
-    }
+    auto split_of = [&](int u) {  // last split with bnd <= u
+      int lo = 0, hi = p.n_split - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_bnd[mid] <= u) lo = mid; else hi = mid - 1;
+      }
+      return lo;
+    };
+    if (p.upw == 1) {
+      const int lo = split_of(p.NS + w);
 #pragma unroll
-    for (int hh = 0; hh < 4; ++hh)
-      if (hh < p.G4) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
+      for (int hh = 0; hh < 4; ++hh)
+        if (hh < p.G4) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
+    } else {  // a window of several units, each normalised by its own split
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < p.upw && w * p.upw + j < p.W; ++j) {
+        const int uo = w * p.upw + j, lo = split_of(p.NS + uo);
+#pragma unroll
+        for (int hh = 0; hh < 4; ++hh) sum[hh] += ms[(int64_t)hh * p.W + uo] * s_f[hh][lo];
+      }
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh)
+        if (hh < p.G4) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + sum[hh];
+    }
   }
 }
 
@@ -905,7 +922,7 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
   decode_mma_kernel<T, D><<<dim3(p.n_split, p.Hv, p.B), kThreads, C::kSmemBytes, stream>>>(p);
   SKV_CHECK_LAUNCH();
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(p.scores ? max(1, ceil_div(p.W, kMergeWindows)) : 1, p.Hv, p.B);
+  cfg.gridDim = dim3(p.scores ? max(1, ceil_div(p.Ww, kMergeWindows)) : 1, p.Hv, p.B);
   cfg.blockDim = dim3(kMergeThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
@@ -932,7 +949,7 @@ int head_groups(const skv_layer_desc* L) {
 
 MmaWs mma_ws(const skv_layer_desc* L, int T) {
   MmaWs w{};
-  const int W = T > L->num_sink ? (T - L->num_sink + L->window_size - 1) / L->window_size : 0;
+  const int W = T > L->num_sink ? (T - L->num_sink + kPageTokens - 1) / kPageTokens : 0;  // units
   const int Hv = head_groups(L);
   w.part = align_up((size_t)L->batch * Hv * kMaxSplits * 4 * (L->head_dim + 2) * 4, 256);
   w.mass = align_up((size_t)L->batch * Hv * 4 * (W > 0 ? W : 1) * 4, 256);
@@ -946,7 +963,7 @@ bool decode_mma_supported(const skv_layer_desc* L) {
   const int G = L->num_q_heads / L->num_kv_heads;
   return (L->kv_dtype == SKV_F16 || L->kv_dtype == SKV_BF16) && (L->head_dim == 64 || L->head_dim == 128) &&
          (G == 1 || G == 2 || G == 4 || G == 8) && L->num_q_heads == G * L->num_kv_heads &&
-         L->window_size == kPageTokens && L->fp_capacity % 8 == 0;
+         L->window_size % kPageTokens == 0 && L->fp_capacity % 8 == 0;
 }
 
 // Lengths the split plan covers: at least one full tile, at most
@@ -986,6 +1003,8 @@ int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, in
   p.rest = T > p.s ? T - p.s - tier_pages * kPageTokens : 0;
   p.U = p.NS + p.n_tp + ceil_div(p.rest, kPageTokens);
   p.W = T > p.s ? (T - p.s + kPageTokens - 1) / kPageTokens : 0;
+  p.upw = L->window_size / kPageTokens;
+  p.Ww = T > p.s ? (T - p.s + L->window_size - 1) / L->window_size : 0;
   p.scale_log2 = scaling * kLog2e;
   p.rope_rows = L->rope_positions;
   if (p.U == 0) return SKV_ERR_INVALID_ARG;

@@ -123,6 +123,50 @@ def test_decode_matches_oracle(dt, D, G, S):
     assert np.all(mass.sum(-1) <= 1 + 1e-4)
 
 
+@pytest.mark.parametrize("dt,ws,G", [("f16", 16, 4), ("bf16", 32, 8), ("f16", 24, 2)])
+def test_decode_window_sizes_match_oracle(dt, ws, G):
+    """Windows of several 8-token units on the tensor-core path: the kernel
+    keeps the mass of every unit, the merge sums a window's units."""
+    g = torch.Generator().manual_seed(ws + G)
+    B, Hkv, D, S = 2, 2, 64, 1203
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, S + 64)
+    cache = make_cache(dt, B, Hkv, Hq, D, S, 1, cos, sin, ws=ws)
+    k, v = rand((B, Hkv, S, D), dt, g), rand((B, Hkv, S, D), dt, g)
+    q = rand((B, Hq, D), dt, g, scale=2.0)
+    cache.update(k.to(DEV), v.to(DEV), 0)
+    st = cache._states[0]
+    nw = math.ceil((S - 4) / ws)
+    before = to_np(st.sides[st.cur].scores[:, :, :nw])
+    out = cache.decode_attention(0, q.to(DEV)[:, :, None, :], D ** -0.5)
+    ref_out, ref_mass = O.tiered_decode_attention(
+        to_np(q), to_np(k)[:, :, :4], to_np(v)[:, :, :4], None, None, to_np(k)[:, :, 4:],
+        to_np(v)[:, :, 4:], 4, ws, D ** -0.5)
+    assert_out_close(to_np(out[:, 0]), ref_out, dt, "decode")
+    np.testing.assert_allclose(to_np(st.window_scores) - before, ref_mass, rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("dt,ws", [("f16", 16), ("bf16", 16)])
+def test_int4_tier_window_16(dt, ws):
+    """int4 tier with two pages per window: eviction state bit-exact, decode
+    output within tolerance, across three evictions."""
+    n_checked = 0
+    for kind, *rest in _drive_pair(dt, tier=True, P=803, steps=49, seed=5, ws=ws):
+        if kind == "evict":
+            cache, oc = rest
+            st = cache._states[0]
+            assert st.tier_pages * 8 == oc.n_tier_tokens
+            for a, b in zip(tier_codes(cache), oc.tier_codes):
+                np.testing.assert_array_equal(a, b)
+            np.testing.assert_array_equal(to_np(st.window_scores), oc.window_scores)
+            np.testing.assert_array_equal(to_np(st.original_window_ids), oc.original_window_ids)
+            n_checked += 1
+        else:
+            out, ref_out, t = rest[0][:3]
+            assert_out_close(to_np(out[:, 0]), ref_out, dt, f"step {t}")
+    assert n_checked == 3
+
+
 # -- int4 pages ---------------------------------------------------------------------------
 
 @pytest.mark.parametrize("dt,D", [("f16", 64), ("bf16", 128), ("f32", 32)])
@@ -158,20 +202,20 @@ def test_pack_pages_bit_exact(dt, D):
 
 # -- eviction -----------------------------------------------------------------------------
 
-def _drive_pair(dt, tier, B=3, Hkv=2, G=4, D=64, P=203, steps=30, seed=0, budget=0.4, local=0.25):
+def _drive_pair(dt, tier, B=3, Hkv=2, G=4, D=64, P=203, steps=30, seed=0, budget=0.4, local=0.25, ws=8):
     """Drive the GPU cache and the oracle cache with identical K/V; scores
     come from the GPU decode kernel each step and are fed to both."""
     g = torch.Generator().manual_seed(seed)
     Hq = Hkv * G
     cos, sin = rope_tables(5e5, D, P + steps + 64)
-    cache = make_cache(dt, B, Hkv, Hq, D, P, steps, cos, sin, budget=budget, local=local, tier=tier)
+    cache = make_cache(dt, B, Hkv, Hq, D, P, steps, cos, sin, ws=ws, budget=budget, local=local, tier=tier)
     r = cache.resolved
-    oc = O.OracleCache(O.resolve(8, 4, local, budget, P, Hkv, D, O.DTYPE_SIZES[dt], steps), dt, cos, sin,
+    oc = O.OracleCache(O.resolve(ws, 4, local, budget, P, Hkv, D, O.DTYPE_SIZES[dt], steps), dt, cos, sin,
                        tier=tier)
     k, v = rand((B, Hkv, P, D), dt, g), rand((B, Hkv, P, D), dt, g)
     cache.update(k.to(DEV), v.to(DEV), 0)
     oc.update(to_np(k), to_np(v), None)
-    scores = O.compute_window_scores(np.random.default_rng(seed).random((B, Hq, 1, P)).astype(np.float32), 4, 8)
+    scores = O.compute_window_scores(np.random.default_rng(seed).random((B, Hq, 1, P)).astype(np.float32), 4, ws)
     st = cache._states[0]
     st.sides[st.cur].scores[:, :, : scores.shape[-1]] = torch.from_numpy(scores).to(DEV)
     st.has_scores, st.W, st.next_window_id = True, scores.shape[-1], scores.shape[-1]
@@ -202,7 +246,7 @@ def _drive_pair(dt, tier, B=3, Hkv=2, G=4, D=64, P=203, steps=30, seed=0, budget
         if W_new > W_old:
             oc.add_scores(np.zeros(acc.shape[:2] + (W_new,), np.float32))
         oc.window_scores = acc.copy()
-    assert evictions == (steps - 1) // 8
+    assert evictions == (steps - 1) // ws
 
 
 @pytest.mark.parametrize("dt,G", [("f32", 4), ("bf16", 4), ("f16", 4), ("f16", 8), ("bf16", 2)])
