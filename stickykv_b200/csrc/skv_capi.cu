@@ -42,8 +42,6 @@ static int check_layer(const skv_layer_desc* L) {
   if (L->batch <= 0 || L->num_kv_heads <= 0 || L->num_q_heads <= 0 || L->head_dim <= 0)
     return SKV_ERR_INVALID_ARG;
   if (L->num_q_heads % L->num_kv_heads) return SKV_ERR_INVALID_ARG;
-  const int G = L->num_q_heads / L->num_kv_heads;
-  if (G != 1 && G != 2 && G != 4 && G != 8) return SKV_ERR_UNSUPPORTED;
   if (L->head_dim != 16 && L->head_dim != 32 && L->head_dim != 64 && L->head_dim != 128)
     return SKV_ERR_UNSUPPORTED;
   if (elt_size(L->kv_dtype) == 0) return SKV_ERR_UNSUPPORTED;
@@ -168,10 +166,19 @@ size_t skv_decode_workspace_size(const skv_layer_desc* L, int32_t T) {
   return a;
 }
 
+// The tensor-core decode takes fp16/bf16 at head_dim 64/128 and any GQA
+// ratio; the portable decode takes every dtype and head_dim at GQA 1/2/4/8.
+static bool decode_kernel_exists(const skv_layer_desc* L, int32_t T) {
+  if (decode_mma_supported(L) && decode_mma_length_ok(T)) return true;
+  const int G = L->num_q_heads / L->num_kv_heads;
+  return G == 1 || G == 2 || G == 4 || G == 8;
+}
+
 static int check_decode(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,
                         float* scores, int32_t scores_cap, void* ws, size_t ws_bytes) {
   int rc = check_layer(L);
   if (rc) return rc;
+  if (T > 0 && !decode_kernel_exists(L, T)) return SKV_ERR_UNSUPPORTED;
   if (T <= 0 || !q || !out) return SKV_ERR_INVALID_ARG;
   if ((rc = check_counts(L, T, tier_pages))) return rc;
   const Geometry g = geometry(L, T, tier_pages);

@@ -1,5 +1,5 @@
 // Tensor-core decode attention with fused window mass (fp16/bf16 KV,
-// window_size a multiple of 8, 1, 2, 4 or 8 query heads per KV head,
+// window_size a multiple of 8, any number of query heads per KV head,
 // head_dim 64 or 128).
 //
 // Same contract as the portable path (skv_decode_generic.cu): replaces the
@@ -13,9 +13,10 @@
 // window_size 8): the kernel records the mass of every unit, the merge sums
 // a window's units.  A tile is two consecutive units (16 tokens).
 //
-// Query heads are handled in groups of four MMA columns: GQA 4 is one group
-// per kv head, GQA 8 two (each reads the kv head's cache once), GQA 1 and 2 one
-// group whose spare columns carry a zero query and are never stored.
+// Query heads are handled in groups of four MMA columns, ceil(G / 4) groups
+// per kv head (each reads the kv head's cache once); the spare columns of a
+// short group (GQA 1, 2, 3, 5, 6, 7 ...) carry a zero query and are never
+// stored.
 //
 // Work split: one CTA per (row, head group, unit range); ranges are balanced by
 // an estimated per-tile cost.  Each of the 4 warps takes a contiguous run of
@@ -96,11 +97,11 @@ struct MmaParams {
   int64_t q_sb, q_sh, o_sb, o_sh, kn_sb, kn_sh;
   int new_slot;       // fp slot of the appended token
   int B, Hkv, cap, page_cap, scores_cap, n_split;
-  // query-head groups: the kernel works on Hv groups of 4 query heads.  GQA 8
-  // splits each kv head into rep = 2 groups (its K/V read once per group);
-  // GQA 1 and 2 give each kv head one group of G4 = G heads, the remaining
-  // columns carry a zero query and are never stored.
-  int Hq, Hv, rep, G4;
+  // query-head groups: the kernel works on Hv groups of up to 4 query heads,
+  // ngrp = ceil(G / 4) per kv head (its K/V read once per group); group j of
+  // kv head r holds query heads r*G + 4j ... + min(4, G - 4j) - 1, and the
+  // spare columns of a short group carry a zero query and are never stored.
+  int Hq, Hv, G, ngrp;
   int s, s_eff, s_pad, NS, n_tp, rest, U, W, rope_rows;
   int upw, Ww;  // 8-token units per window (window_size / 8) and windows; W counts units
   float scale_log2;
@@ -217,7 +218,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   constexpr float kThresh = 8.f;                          // lazy rescale margin (log2 domain)
   extern __shared__ __align__(128) unsigned char smem[];
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;  // kh: query-head group
-  const int kr = kh / p.rep;                                       // its kv head
+  const int kr = kh / p.ngrp;                                      // its kv head
+  const int hbase = kr * p.G + 4 * (kh - kr * p.ngrp);             // its first query head
+  const int nlive = min(4, p.G - (hbase - kr * p.G));              // its query heads
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int u0 = p.bnd[split], u1 = p.bnd[split + 1];
@@ -277,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   const uint32_t vs_off = page_v_scales_off(D) + t * NW * 8;
 
   // query of head (g & 3) in B-fragment order: d = 16kb + 2t + {0,1,8,9}
-  const bool q_live = (g & 3) < p.G4;  // columns past the group's heads carry a zero query
-  const T* qp = (const T*)p.q + b * p.q_sb + (kh * p.G4 + (q_live ? (g & 3) : 0)) * p.q_sh;
+  const bool q_live = (g & 3) < nlive;  // columns past the group's heads carry a zero query
+  const T* qp = (const T*)p.q + b * p.q_sb + (hbase + (q_live ? (g & 3) : 0)) * p.q_sh;
   const uint32_t q_bits = q_live ? 0xFFFFFFFFu : 0u;
   // query rotated to the page start of this thread's column (int4 columns)
   float rq[KB][4];
@@ -769,18 +772,20 @@ constexpr int kMergeWindows = kMergePer * kMergeThreads;   // windows per block
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const __grid_constant__ MmaParams p) {
   const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;  // kh: query-head group
+  const int kr = kh / p.ngrp, hbase = kr * p.G + 4 * (kh - kr * p.ngrp);
+  const int nlive = min(4, p.G - (hbase - kr * p.G));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float s_f[4][kMaxSplits];   // split factor / L per head
   __shared__ int s_bnd[kMaxSplits + 1];
   const int w0 = chunk * kMergeWindows, w_end = min(p.Ww, w0 + kMergeWindows);
-  float* acc = p.scores ? p.scores + ((int64_t)b * p.Hq + kh * p.G4) * p.scores_cap : nullptr;
+  float* acc = p.scores ? p.scores + ((int64_t)b * p.Hq + hbase) * p.scores_cap : nullptr;
   float av[4][kMergePer];
 #pragma unroll
   for (int hh = 0; hh < 4; ++hh)
 #pragma unroll
     for (int k = 0; k < kMergePer; ++k) {
       const int w = w0 + threadIdx.x + k * kMergeThreads;
-      av[hh][k] = (acc && w < w_end && hh < p.G4) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
+      av[hh][k] = (acc && w < w_end && hh < nlive) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
     }
   for (int j = threadIdx.x; j <= p.n_split; j += kMergeThreads) s_bnd[j] = p.bnd[j];
   grid_dependency_wait();
@@ -837,7 +842,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       for (int sp = 0; sp < kPre; ++sp) o += s_f[hh][sp < p.n_split ? sp : 0] * ov[q][sp];
 #pragma unroll 8
       for (int sp = kPre; sp < p.n_split; ++sp) o += s_f[hh][sp] * part[(sp * 4 + hh) * (D + 2) + c];
-      if (hh < p.G4) st_f32((T*)p.out + b * p.o_sb + (kh * p.G4 + hh) * p.o_sh + c, o);
+      if (hh < nlive) st_f32((T*)p.out + b * p.o_sb + (hbase + hh) * p.o_sh + c, o);
     }
   }
   if (acc == nullptr) return;
@@ -857,7 +862,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       const int lo = split_of(p.NS + w);
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh)
-        if (hh < p.G4) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
+        if (hh < nlive) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
     } else {  // a window of several units, each normalised by its own split
       float sum[4] = {0.f, 0.f, 0.f, 0.f};
       for (int j = 0; j < p.upw && w * p.upw + j < p.W; ++j) {
@@ -867,7 +872,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       }
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh)
-        if (hh < p.G4) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + sum[hh];
+        if (hh < nlive) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + sum[hh];
     }
   }
 }
@@ -942,9 +947,10 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
 struct MmaWs {
   size_t part, mass, total;
 };
-// query-head groups of 4 columns: GQA 8 gives two per kv head, GQA 1/2/4 one
+// query-head groups of up to 4 MMA columns: ceil(G / 4) per kv head
 int head_groups(const skv_layer_desc* L) {
-  return L->num_kv_heads * (L->num_q_heads > 4 * L->num_kv_heads ? L->num_q_heads / (4 * L->num_kv_heads) : 1);
+  const int G = L->num_q_heads / L->num_kv_heads;
+  return L->num_kv_heads * ((G + 3) / 4);
 }
 
 MmaWs mma_ws(const skv_layer_desc* L, int T) {
@@ -962,7 +968,7 @@ MmaWs mma_ws(const skv_layer_desc* L, int T) {
 bool decode_mma_supported(const skv_layer_desc* L) {
   const int G = L->num_q_heads / L->num_kv_heads;
   return (L->kv_dtype == SKV_F16 || L->kv_dtype == SKV_BF16) && (L->head_dim == 64 || L->head_dim == 128) &&
-         (G == 1 || G == 2 || G == 4 || G == 8) && L->num_q_heads == G * L->num_kv_heads &&
+         G >= 1 && L->num_q_heads == G * L->num_kv_heads &&
          L->window_size % kPageTokens == 0 && L->fp_capacity % 8 == 0;
 }
 
@@ -993,9 +999,9 @@ int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, in
   p.q_sb = q_sb; p.q_sh = q_sh; p.o_sb = o_sb; p.o_sh = o_sh;
   p.B = L->batch; p.Hkv = L->num_kv_heads; p.cap = L->fp_capacity; p.page_cap = L->tier_page_capacity;
   p.Hq = L->num_q_heads;
-  p.Hv = head_groups(L);
-  p.rep = p.Hv / p.Hkv;
-  p.G4 = p.Hq / p.Hv;
+  p.G = p.Hq / p.Hkv;
+  p.ngrp = (p.G + 3) / 4;
+  p.Hv = p.Hkv * p.ngrp;
   p.scores_cap = scores_cap;
   p.s = L->num_sink; p.s_pad = L->sink_pad; p.n_tp = tier_pages;
   p.s_eff = T < p.s ? T : p.s;

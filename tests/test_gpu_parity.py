@@ -100,7 +100,8 @@ def test_decode_matches_reference_eager_golden(dt):
 
 @pytest.mark.parametrize("dt,D,G,S", [("f32", 64, 2, 300), ("f16", 64, 4, 1000), ("bf16", 128, 4, 777),
                                       ("f16", 128, 8, 64), ("bf16", 64, 1, 2049), ("f16", 32, 4, 5000),
-                                      ("f16", 64, 2, 1500), ("bf16", 64, 8, 3001), ("f16", 128, 1, 900)])
+                                      ("f16", 64, 2, 1500), ("bf16", 64, 8, 3001), ("f16", 128, 1, 900),
+                                      ("f16", 64, 7, 1100), ("bf16", 128, 3, 600), ("f16", 64, 6, 2500)])
 def test_decode_matches_oracle(dt, D, G, S):
     g = torch.Generator().manual_seed(S + D)
     B, Hkv = 3, 2
@@ -249,7 +250,7 @@ def _drive_pair(dt, tier, B=3, Hkv=2, G=4, D=64, P=203, steps=30, seed=0, budget
     assert evictions == (steps - 1) // ws
 
 
-@pytest.mark.parametrize("dt,G", [("f32", 4), ("bf16", 4), ("f16", 4), ("f16", 8), ("bf16", 2)])
+@pytest.mark.parametrize("dt,G", [("f32", 4), ("bf16", 4), ("f16", 4), ("f16", 8), ("bf16", 2), ("bf16", 7)])
 def test_reference_mode_eviction_bit_exact(dt, G):
     for kind, *rest in _drive_pair(dt, tier=False, G=G):
         if kind == "evict":
@@ -264,11 +265,11 @@ def test_reference_mode_eviction_bit_exact(dt, G):
             assert_out_close(to_np(out[:, 0]), ref_out, dt, f"step {t}")
 
 
-@pytest.mark.parametrize("dt,G", [("f16", 4), ("bf16", 4), ("f16", 8), ("bf16", 2), ("f16", 1)])
+@pytest.mark.parametrize("dt,G", [("f16", 4), ("bf16", 4), ("f16", 8), ("bf16", 2), ("f16", 1), ("f16", 6)])
 def test_int4_tier_eviction_and_decode(dt, G):
-    """int4 tier, every GQA ratio the tensor-core decode takes (head groups
-    of four columns: one per kv head, two at GQA 8, spare columns at GQA 1
-    and 2)."""
+    """int4 tier at several GQA ratios (query heads in groups of four MMA
+    columns: one group per kv head up to GQA 4, two above; spare columns in
+    short groups)."""
     n_checked = 0
     for kind, *rest in _drive_pair(dt, tier=True, G=G, P=403, steps=34, seed=3):
         if kind == "evict":
@@ -328,7 +329,7 @@ def test_prefill_scores_match_reference_golden():
 
 @pytest.mark.parametrize("dt,D,G,T", [("f16", 64, 4, 333), ("bf16", 64, 4, 333), ("bf16", 128, 2, 700),
                                        ("f16", 128, 8, 129), ("f16", 64, 1, 64), ("f16", 64, 2, 256),
-                                       ("bf16", 128, 4, 1100)])
+                                       ("bf16", 128, 4, 1100), ("bf16", 64, 7, 300)])
 def test_prefill_matches_oracle(dt, D, G, T):
     """Tensor-core prefill (fp16/bf16, head_dim 64/128): output against torch
     fp32 attention, prompt window scores against the oracle; partial last
