@@ -47,3 +47,46 @@ def test_cfg1_greedy_generation_matches_reference():
         want[..., : pend.shape[-1]] += pend[..., : want.shape[-1]]
         np.testing.assert_allclose(st.window_scores.float().cpu().numpy(), want, rtol=1e-5, atol=1e-6)
     assert model.config._attn_implementation == "eager"  # restored by remove()
+
+
+def test_qwen2_gqa7_matches_transformers_attention_without_eviction():
+    """A 2-layer Qwen2-shaped fp16 model with 14 query and 2 kv heads (GQA 7,
+    head_dim 64, the tensor-core decode's head groups of 4 + 3) through this
+    package's hooks, with a budget that never evicts: every step's logits
+    match transformers' own cache and eager attention on the same tokens."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from stickykv_b200.cache_factory import get_cache_classes
+    cfg = Qwen2Config(vocab_size=32000, hidden_size=896, intermediate_size=1024, num_hidden_layers=2,
+                      num_attention_heads=14, num_key_value_heads=2, max_position_embeddings=4096,
+                      rope_theta=1e6, tie_word_embeddings=True)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    model = Qwen2ForCausalLM(cfg).to(torch.float16).cuda().eval()
+    P, steps = 512, 16
+    ids = torch.randint(0, 32000, (2, P), generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad():
+        out = model(input_ids=ids, use_cache=True)
+        past = out.past_key_values
+        toks, ref = [out.logits[:, -1:].argmax(-1)], [out.logits[:, -1].float()]
+        for _ in range(steps - 1):
+            out = model(input_ids=toks[-1], past_key_values=past, use_cache=True)
+            past = out.past_key_values
+            toks.append(out.logits[:, -1:].argmax(-1))
+            ref.append(out.logits[:, -1].float())
+    Cache, Config, install = get_cache_classes("b200")
+    wcfg = Config(window_size=8, num_sink_tokens=4, local_window_size=0.25, cache_budget=1.0)
+    cache = Cache(wcfg, P, model.config, torch.float16, model.model.rotary_emb, 2, steps)
+    handles = install(model, cache, wcfg)
+    try:
+        with torch.no_grad():
+            out = model(input_ids=ids, past_key_values=cache, use_cache=True)
+            got = [out.logits[:, -1].float()]
+            for t in range(steps - 1):
+                out = model(input_ids=toks[t], past_key_values=cache, use_cache=True)
+                got.append(out.logits[:, -1].float())
+    finally:
+        handles.remove()
+    for t, (a, b) in enumerate(zip(got, ref)):
+        torch.testing.assert_close(a, b, atol=2e-2, rtol=0, msg=f"step {t}")
+    assert cache.get_seq_length(0) == P + steps - 1
