@@ -446,23 +446,33 @@ __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) 
       sn[e / 2] = T2{Elt<T>::from_f32(tsn[e]), Elt<T>::from_f32(tsn[e + 1])};
     }
     union V2 { uint4 u; T2 e[VE / 2]; };
+    constexpr int HB = 4;  // kv heads whose loads are in flight together
+    const int64_t hs_src = (int64_t)p.fp_cap_src * D, hs_dst = (int64_t)p.fp_cap_dst * D;
+    const T* ks0 = (const T*)p.k_src + ((int64_t)b * p.Hkv * p.fp_cap_src + so_slot) * D + c0;
+    T* kd0 = (T*)p.k_dst + ((int64_t)b * p.Hkv * p.fp_cap_dst + sd_slot) * D + c0;
 #pragma unroll 1
-    for (int h = 0; h < p.Hkv; ++h) {
-      const T* ks = (const T*)p.k_src + (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
-      T* kd = (T*)p.k_dst + (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
-      V2 x, y;
-      x.u = *reinterpret_cast<const uint4*>(ks + c0);
-      y.u = *reinterpret_cast<const uint4*>(ks + c0 + half);
+    for (int h0 = 0; h0 < p.Hkv; h0 += HB) {
+      V2 x[HB], y[HB];
 #pragma unroll
-      for (int e = 0; e < VE / 2; ++e) {
-        // strip (cos, -sin), then re-apply (cos, sin)
-        const T2 ux = __hadd2_rn(__hmul2_rn(x.e[e], co[e]), __hmul2_rn(y.e[e], so[e]));
-        const T2 uy = __hsub2_rn(__hmul2_rn(y.e[e], co[e]), __hmul2_rn(x.e[e], so[e]));
-        x.e[e] = __hsub2_rn(__hmul2_rn(ux, cn[e]), __hmul2_rn(uy, sn[e]));
-        y.e[e] = __hadd2_rn(__hmul2_rn(uy, cn[e]), __hmul2_rn(ux, sn[e]));
+      for (int j = 0; j < HB; ++j)
+        if (h0 + j < p.Hkv) {
+          x[j].u = *reinterpret_cast<const uint4*>(ks0 + (h0 + j) * hs_src);
+          y[j].u = *reinterpret_cast<const uint4*>(ks0 + (h0 + j) * hs_src + half);
+        }
+#pragma unroll
+      for (int j = 0; j < HB; ++j) {
+        if (h0 + j >= p.Hkv) break;
+#pragma unroll
+        for (int e = 0; e < VE / 2; ++e) {
+          // strip (cos, -sin), then re-apply (cos, sin)
+          const T2 ux = __hadd2_rn(__hmul2_rn(x[j].e[e], co[e]), __hmul2_rn(y[j].e[e], so[e]));
+          const T2 uy = __hsub2_rn(__hmul2_rn(y[j].e[e], co[e]), __hmul2_rn(x[j].e[e], so[e]));
+          x[j].e[e] = __hsub2_rn(__hmul2_rn(ux, cn[e]), __hmul2_rn(uy, sn[e]));
+          y[j].e[e] = __hadd2_rn(__hmul2_rn(uy, cn[e]), __hmul2_rn(ux, sn[e]));
+        }
+        *reinterpret_cast<uint4*>(kd0 + (h0 + j) * hs_dst) = x[j].u;
+        *reinterpret_cast<uint4*>(kd0 + (h0 + j) * hs_dst + half) = y[j].u;
       }
-      *reinterpret_cast<uint4*>(kd + c0) = x.u;
-      *reinterpret_cast<uint4*>(kd + c0 + half) = y.u;
     }
   } else {
     float co[VE], so[VE], cn[VE], sn[VE];
