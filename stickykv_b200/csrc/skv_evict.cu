@@ -91,9 +91,16 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   if (partial) {
     const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
     for (int w = tid; w < E; w += nt) {
-      // heads summed in order; loads issued 16 at a time
+      // heads summed in order; loads issued 32 at a time
       float acc = 0.f;
       int h = 0;
+      for (; h + 32 <= p.Hq; h += 32) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc = __fadd_rn(acc, v[i]);
+      }
       for (; h + 16 <= p.Hq; h += 16) {
         float v[16];
 #pragma unroll
