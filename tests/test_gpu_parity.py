@@ -168,6 +168,39 @@ def test_int4_tier_window_16(dt, ws):
     assert n_checked == 3
 
 
+def _random_geometries(n, seed=2024):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        out.append((str(rng.choice(["f16", "bf16"])), int(rng.choice([64, 128])), int(rng.integers(1, 9)),
+                    int(rng.choice([8, 16])), int(rng.integers(17, 2600)), int(rng.integers(1, 3)),
+                    int(rng.integers(1, 3))))
+    return out
+
+
+@pytest.mark.parametrize("dt,D,G,ws,S,B,Hkv", _random_geometries(12))
+def test_decode_random_geometries(dt, D, G, ws, S, B, Hkv):
+    """Seeded random geometries (dtype, head_dim, GQA 1-8, window 8/16, odd
+    lengths, 1-2 rows and kv heads) on the tensor-core decode against the
+    oracle: output and window mass."""
+    g = torch.Generator().manual_seed(S * 7 + G)
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, S + 64)
+    cache = make_cache(dt, B, Hkv, Hq, D, S, 1, cos, sin, ws=ws)
+    k, v = rand((B, Hkv, S, D), dt, g), rand((B, Hkv, S, D), dt, g)
+    q = rand((B, Hq, D), dt, g, scale=2.0)
+    cache.update(k.to(DEV), v.to(DEV), 0)
+    st = cache._states[0]
+    nw = math.ceil((S - 4) / ws)
+    before = to_np(st.sides[st.cur].scores[:, :, :nw])
+    out = cache.decode_attention(0, q.to(DEV)[:, :, None, :], D ** -0.5)
+    ref_out, ref_mass = O.tiered_decode_attention(
+        to_np(q), to_np(k)[:, :, :4], to_np(v)[:, :, :4], None, None, to_np(k)[:, :, 4:],
+        to_np(v)[:, :, 4:], 4, ws, D ** -0.5)
+    assert_out_close(to_np(out[:, 0]), ref_out, dt, "decode")
+    np.testing.assert_allclose(to_np(st.window_scores) - before, ref_mass, rtol=1e-4, atol=1e-6)
+
+
 # -- int4 pages ---------------------------------------------------------------------------
 
 @pytest.mark.parametrize("dt,D", [("f16", 64), ("bf16", 128), ("f32", 32)])
