@@ -327,6 +327,28 @@ def test_int4_tier_eviction_and_decode(dt, G):
 
 
 
+@pytest.mark.parametrize("dt,G,ws,D", [("bf16", 5, 8, 128), ("f16", 3, 16, 64), ("bf16", 6, 8, 64)])
+def test_int4_tier_other_geometries(dt, G, ws, D):
+    """int4 tier at GQA 3/5/6, head_dim 64/128 and windows of 8/16 tokens:
+    tier codes, scores and ids bit-exact after each eviction, decode output
+    within tolerance every step."""
+    n_checked = 0
+    for kind, *rest in _drive_pair(dt, tier=True, G=G, D=D, ws=ws, P=611, steps=2 * ws + 1, seed=G + ws):
+        if kind == "evict":
+            cache, oc = rest
+            st = cache._states[0]
+            assert st.tier_pages * 8 == oc.n_tier_tokens
+            for a, b in zip(tier_codes(cache), oc.tier_codes):
+                np.testing.assert_array_equal(a, b)
+            np.testing.assert_array_equal(to_np(st.window_scores), oc.window_scores)
+            np.testing.assert_array_equal(to_np(st.original_window_ids), oc.original_window_ids)
+            n_checked += 1
+        else:
+            out, ref_out, t = rest[0][:3]
+            assert_out_close(to_np(out[:, 0]), ref_out, dt, f"step {t}")
+    assert n_checked == 2
+
+
 @pytest.mark.parametrize("P", [5000, 6000])
 def test_int4_tier_decode_long_single_head(P):
     """One (row, kv head) with thousands of retained tokens: the decode splits
