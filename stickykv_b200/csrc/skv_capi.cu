@@ -167,11 +167,11 @@ size_t skv_decode_workspace_size(const skv_layer_desc* L, int32_t T) {
 }
 
 // The tensor-core decode takes fp16/bf16 at head_dim 64/128 and any GQA
-// ratio; the portable decode takes every dtype and head_dim at GQA 1/2/4/8.
+// ratio; the portable decode takes every dtype and head_dim at GQA 1 to 8.
 static bool decode_kernel_exists(const skv_layer_desc* L, int32_t T) {
   if (decode_mma_supported(L) && decode_mma_length_ok(T)) return true;
   const int G = L->num_q_heads / L->num_kv_heads;
-  return G == 1 || G == 2 || G == 4 || G == 8;
+  return G >= 1 && G <= 8;
 }
 
 static int check_decode(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,

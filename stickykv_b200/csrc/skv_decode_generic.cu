@@ -251,7 +251,11 @@ int dispatch_g(DecodeParams& p, int G, cudaStream_t s) {
   switch (G) {
     case 1: return launch_decode_generic<T, D, 1>(p, s);
     case 2: return launch_decode_generic<T, D, 2>(p, s);
+    case 3: return launch_decode_generic<T, D, 3>(p, s);
     case 4: return launch_decode_generic<T, D, 4>(p, s);
+    case 5: return launch_decode_generic<T, D, 5>(p, s);
+    case 6: return launch_decode_generic<T, D, 6>(p, s);
+    case 7: return launch_decode_generic<T, D, 7>(p, s);
     case 8: return launch_decode_generic<T, D, 8>(p, s);
   }
   return SKV_ERR_UNSUPPORTED;

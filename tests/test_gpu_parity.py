@@ -101,7 +101,8 @@ def test_decode_matches_reference_eager_golden(dt):
 @pytest.mark.parametrize("dt,D,G,S", [("f32", 64, 2, 300), ("f16", 64, 4, 1000), ("bf16", 128, 4, 777),
                                       ("f16", 128, 8, 64), ("bf16", 64, 1, 2049), ("f16", 32, 4, 5000),
                                       ("f16", 64, 2, 1500), ("bf16", 64, 8, 3001), ("f16", 128, 1, 900),
-                                      ("f16", 64, 7, 1100), ("bf16", 128, 3, 600), ("f16", 64, 6, 2500)])
+                                      ("f16", 64, 7, 1100), ("bf16", 128, 3, 600), ("f16", 64, 6, 2500),
+                                      ("f32", 64, 7, 500), ("f32", 32, 3, 700), ("f16", 32, 5, 900)])
 def test_decode_matches_oracle(dt, D, G, S):
     g = torch.Generator().manual_seed(S + D)
     B, Hkv = 3, 2
