@@ -367,6 +367,45 @@ def unpack_page(page: np.ndarray, D: int):
     return kc, ks, kz, vc, vs, vz
 
 
+def unpack_pages(pages: np.ndarray, D: int):
+    """Vectorised :func:`unpack_page` over any leading shape: pages
+    [..., page_bytes] uint8 -> (kc, ks, kz, vc, vs, vz) with shapes
+    [..., 8, D] / [..., 8, D/32] (same layout rules as :func:`pack_page`)."""
+    NW = D // QGROUP
+    pages = np.ascontiguousarray(pages, dtype=np.uint8)
+    lead = pages.shape[:-1]
+    o = 0
+    n = PAGE_TOKENS * 4 * NW * 4
+    kw = pages[..., o:o + n].copy().view(np.uint32).reshape(lead + (PAGE_TOKENS, 4, NW)); o += n
+    n = PAGE_TOKENS * NW * 2 * 2
+    ksc = pages[..., o:o + n].copy().view(np.float16).reshape(lead + (PAGE_TOKENS, NW, 2)); o += n
+    n = 4 * 8 * NW * 4
+    vw = pages[..., o:o + n].copy().view(np.uint32).reshape(lead + (4, 8, NW)); o += n
+    n = 4 * NW * 4 * 2
+    vsc = pages[..., o:o + n].copy().view(np.float16).reshape(lead + (4, NW, 4))
+    shifts = (4 * np.arange(8, dtype=np.uint32))
+    knib = ((kw[..., None] >> shifts) & 0xF).astype(np.uint8)   # [..., r, t, w, nibble]
+    vnib = ((vw[..., None] >> shifts) & 0xF).astype(np.uint8)   # [..., t, g, w, nibble]
+    kc = np.zeros(lead + (PAGE_TOKENS, D), np.uint8)
+    vc = np.zeros(lead + (PAGE_TOKENS, D), np.uint8)
+    for t in range(4):
+        for w in range(NW):
+            for i in range(4):
+                ch = 2 * t + 8 * (4 * w + i)
+                kc[..., ch] = knib[..., t, w, i]
+                kc[..., ch + 1] = knib[..., t, w, i + 4]
+                c0 = 8 * (4 * w + i)
+                vc[..., 2 * t, c0:c0 + 8] = vnib[..., t, :, w, i]
+                vc[..., 2 * t + 1, c0:c0 + 8] = vnib[..., t, :, w, i + 4]
+    ks, kz = ksc[..., 0].copy(), ksc[..., 1].copy()
+    vs = np.zeros(lead + (PAGE_TOKENS, NW), np.float16)
+    vz = np.zeros(lead + (PAGE_TOKENS, NW), np.float16)
+    for t in range(4):
+        vs[..., 2 * t, :], vs[..., 2 * t + 1, :] = vsc[..., t, :, 0], vsc[..., t, :, 1]
+        vz[..., 2 * t, :], vz[..., 2 * t + 1, :] = vsc[..., t, :, 2], vsc[..., t, :, 3]
+    return kc, ks, kz, vc, vs, vz
+
+
 def to_page_frame(k: np.ndarray, old_pos: np.ndarray, cos_tab: np.ndarray,
                   sin_tab: np.ndarray, num_sink: int) -> np.ndarray:
     """Post-RoPE key (fp32 of the KV-dtype value) at ``old_pos`` -> the key in
@@ -474,6 +513,46 @@ def tiered_decode_attention(q: np.ndarray, sinks_k: np.ndarray, sinks_v: np.ndar
     p = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
     out = np.einsum("bhs,bhsd->bhd", p, vall).astype(np.float32)
     mass = reduce_token_scores_to_windows(p, s, window_size)
+    return out, mass
+
+
+def tiered_decode_attention_grouped(q: np.ndarray, sinks_k: np.ndarray, sinks_v: np.ndarray,
+                                    tier_k: Optional[np.ndarray], tier_v: Optional[np.ndarray],
+                                    rest_k: np.ndarray, rest_v: np.ndarray, num_sink: int,
+                                    window_size: int, scaling: float, cos_tab=None, sin_tab=None):
+    """:func:`tiered_decode_attention` for long caches: the same math with the
+    query heads grouped per kv head (no ``repeat_kv`` copy of K/V) and the
+    per-page query rotation vectorised, so a 32k-token cache of 16 rows fits
+    in a few hundred MB.  Same arguments and returns."""
+    B, Hq, D = q.shape
+    Hkv = rest_k.shape[1]
+    G = Hq // Hkv
+    h = D // 2
+    qg = q.astype(np.float32).reshape(B, Hkv, G, D)
+    parts, vparts = [], []
+    parts.append(np.einsum("bkgd,bknd->bkgn", qg, sinks_k.astype(np.float32)))
+    vparts.append(sinks_v.astype(np.float32))
+    nt = 0 if tier_k is None else tier_k.shape[2]
+    if nt:
+        npg = nt // PAGE_TOKENS
+        pos = num_sink + PAGE_TOKENS * np.arange(npg)
+        c = cos_tab[pos][:, :h].astype(np.float32)           # [npg, h]
+        s = sin_tab[pos][:, :h].astype(np.float32)
+        x, y = qg[..., None, :h], qg[..., None, h:]           # [B,Hkv,G,1,h]
+        qr = np.concatenate([x * c + y * s, y * c - x * s], axis=-1).astype(np.float32)  # [B,Hkv,G,npg,D]
+        kt = tier_k.astype(np.float32).reshape(B, Hkv, npg, PAGE_TOKENS, D)
+        lt = np.einsum("bkgpd,bkprd->bkgpr", qr, kt).reshape(B, Hkv, G, nt)
+        parts.append(lt)
+        vparts.append(tier_v.astype(np.float32))
+    parts.append(np.einsum("bkgd,bknd->bkgn", qg, rest_k.astype(np.float32)))
+    vparts.append(rest_v.astype(np.float32))
+    logits = np.concatenate(parts, axis=-1).astype(np.float32) * np.float32(scaling)
+    vall = np.concatenate(vparts, axis=2)
+    m = logits.max(axis=-1, keepdims=True)
+    e = np.exp((logits - m).astype(np.float32))
+    p = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+    out = np.einsum("bkgn,bknd->bkgd", p, vall).astype(np.float32).reshape(B, Hq, D)
+    mass = reduce_token_scores_to_windows(p.reshape(B, Hq, -1), num_sink, window_size)
     return out, mass
 
 

@@ -18,6 +18,7 @@ never reads device memory.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import math
 from typing import Any, Dict, List, Optional, Tuple
@@ -45,6 +46,15 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
 
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _on(device: torch.device):
+    """Make ``device`` current for a native call (kernels launch on the
+    current device; the stream passed with them belongs to ``device``).
+    Layers of one model may sit on different GPUs (``device_map``)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 class _Side:
@@ -175,10 +185,11 @@ class WindowedCache(_HFCacheBase):
         self._generation_step: List[int] = [0] * num_layers
         self._prefill_done: List[bool] = [False] * num_layers
         self.cache_kwargs: Dict[int, Dict[str, Any]] = {i: {} for i in range(num_layers)}
-        self._rope: Optional[Tuple[Tensor, Tensor]] = None
-        self._rope_positions = 0
-        self._ws: Optional[Tensor] = None
-        self._retained: Optional[Tensor] = None
+        # per device: layers placed on several GPUs each use their own
+        self._rope: Dict[torch.device, Tuple[Tensor, Tensor]] = {}
+        self._rope_positions: Dict[torch.device, int] = {}
+        self._ws: Dict[torch.device, Tensor] = {}
+        self._retained: Dict[torch.device, Tensor] = {}
         self.layers = []
 
     # -- HF Cache surface ---------------------------------------------------------------
@@ -284,9 +295,10 @@ class WindowedCache(_HFCacheBase):
         st.allocated = True
 
     def _ensure_rope(self, n: int, D: int, dev: torch.device) -> None:
-        if self._rope is not None and self._rope_positions >= n:
+        have = self._rope_positions.get(dev, 0)
+        if have >= n:
             return
-        n = max(n, 2 * self._rope_positions)
+        n = max(n, 2 * have)
         x = torch.zeros(1, 1, 1, D, dtype=torch.float32, device=dev)
         pos = torch.arange(n, device=dev).unsqueeze(0)
         with torch.no_grad():
@@ -296,8 +308,8 @@ class WindowedCache(_HFCacheBase):
         if cos.shape[-1] != D or not torch.equal(cos[:, : D // 2], cos[:, D // 2:]) or \
                 not torch.equal(sin[:, : D // 2], sin[:, D // 2:]):
             raise NotImplementedError("rotary module must use the rotate-half layout cat(f, f)")
-        self._rope = (cos[:, : D // 2].contiguous(), sin[:, : D // 2].contiguous())
-        self._rope_positions = n
+        self._rope[dev] = (cos[:, : D // 2].contiguous(), sin[:, : D // 2].contiguous())
+        self._rope_positions[dev] = n
 
     def _grow_side(self, st: LayerState, side: _Side, need_slots: int) -> None:
         cap = side.k.shape[2]
@@ -311,8 +323,9 @@ class WindowedCache(_HFCacheBase):
             setattr(side, name, new)
 
     def _desc(self, st: LayerState, side: _Side) -> LayerDesc:
+        rope = self._rope[st.device]
         key = (side.k.data_ptr(), side.v.data_ptr(), side.k.shape[2],
-               None if side.table is None else side.table.data_ptr(), self._rope_positions)
+               None if side.table is None else side.table.data_ptr(), rope[0].data_ptr())
         if side.desc_key == key:
             return side.desc
         r = self.resolved
@@ -327,8 +340,8 @@ class WindowedCache(_HFCacheBase):
             d.tier_page_capacity = st.page_cap
             d.tier_pages = st.pages.data_ptr()
             d.tier_table = side.table.data_ptr()
-        d.rope_cos, d.rope_sin = self._rope[0].data_ptr(), self._rope[1].data_ptr()
-        d.rope_positions = self._rope_positions
+        d.rope_cos, d.rope_sin = rope[0].data_ptr(), rope[1].data_ptr()
+        d.rope_positions = self._rope_positions[st.device]
         side.desc, side.desc_key = d, key
         return d
 
@@ -339,9 +352,11 @@ class WindowedCache(_HFCacheBase):
         return (s + 7) // 8 * 8 + (T - s - tier_pages * _lib.PAGE_TOKENS)
 
     def _workspace(self, nbytes: int, device: torch.device) -> Tensor:
-        if self._ws is None or self._ws.numel() < nbytes:
-            self._ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        return self._ws
+        ws = self._ws.get(device)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            self._ws[device] = ws
+        return ws
 
     # -- update (reference cache.py:110-293) ------------------------------------------------
     def update(self, key_states: Tensor, value_states: Tensor, layer_idx: int,
@@ -404,9 +419,10 @@ class WindowedCache(_HFCacheBase):
         k, v = st.pending
         st.pending = None
         d = self._desc(st, st.sides[st.cur])
-        check(lib().skv_append(C.byref(d), st.T - 1, st.tier_pages, k.data_ptr(), v.data_ptr(),
-                               k.stride(0), k.stride(1), k.stride(2), 1, _stream(st.device)),
-              "skv_append")
+        with _on(st.device):
+            check(lib().skv_append(C.byref(d), st.T - 1, st.tier_pages, k.data_ptr(), v.data_ptr(),
+                                   k.stride(0), k.stride(1), k.stride(2), 1, _stream(st.device)),
+                  "skv_append")
 
     def _append(self, st: LayerState, k: Tensor, v: Tensor) -> None:
         n_new = k.shape[2]
@@ -418,9 +434,10 @@ class WindowedCache(_HFCacheBase):
         max_T = st.T + n_new + 2
         self._ensure_rope(max_T + 64, st.D, st.device)
         d = self._desc(st, side)
-        check(lib().skv_append(C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(),
-                               k.stride(0), k.stride(1), k.stride(2), n_new, _stream(st.device)),
-              "skv_append")
+        with _on(st.device):
+            check(lib().skv_append(C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(),
+                                   k.stride(0), k.stride(1), k.stride(2), n_new, _stream(st.device)),
+                  "skv_append")
         st.T += n_new
 
     def _add_scores(self, st: LayerState, new: Tensor) -> None:
@@ -465,9 +482,11 @@ class WindowedCache(_HFCacheBase):
             dst.k = torch.empty(st.B, st.Hkv, -(-2 * need // 8) * 8, st.D, dtype=st.dtype, device=st.device)
             dst.v = torch.empty_like(dst.k)
         want_tel = bool(getattr(self.telemetry, "enabled", False))
+        retained = self._retained.get(st.device)
         if want_tel:
-            if self._retained is None or self._retained.shape != (st.B, st.scores_cap):
-                self._retained = torch.zeros(st.B, st.scores_cap, dtype=torch.int32, device=st.device)
+            if retained is None or retained.shape != (st.B, st.scores_cap):
+                retained = torch.zeros(st.B, st.scores_cap, dtype=torch.int32, device=st.device)
+                self._retained[st.device] = retained
             pre = src.scores[:, :, : st.W].clone()
         a = EvictArgs()
         a.seq_len, a.tier_pages, a.num_windows = st.T, st.tier_pages, st.W
@@ -475,15 +494,16 @@ class WindowedCache(_HFCacheBase):
         a.scores_capacity = st.scores_cap
         a.scores_src, a.scores_dst = src.scores.data_ptr(), dst.scores.data_ptr()
         a.ids_src, a.ids_dst = src.ids.data_ptr(), dst.ids.data_ptr()
-        a.retained_out = self._retained.data_ptr() if want_tel else None
+        a.retained_out = retained.data_ptr() if want_tel else None
         a.next_window_id = st.next_window_id
         ds, dd = self._desc(st, src), self._desc(st, dst)
         nbytes = lib().skv_evict_workspace_size(C.byref(ds), st.W)
         ws = self._workspace(nbytes, st.device)
-        check(lib().skv_evict(C.byref(ds), C.byref(dd), C.byref(a), ws.data_ptr(), ws.numel(),
-                              _stream(st.device)), "skv_evict")
+        with _on(st.device):
+            check(lib().skv_evict(C.byref(ds), C.byref(dd), C.byref(a), ws.data_ptr(), ws.numel(),
+                                  _stream(st.device)), "skv_evict")
         if want_tel:
-            ret = self._retained[:, : plan.retained_windows].long()
+            ret = retained[:, : plan.retained_windows].long()
             self.telemetry.record_scores(layer_idx, step, pre, self._token_indices(ret, st.T))
         st.cur ^= 1
         st.T = plan.seq_len_new
@@ -519,19 +539,20 @@ class WindowedCache(_HFCacheBase):
         ws = self._workspace(st.decode_ws, st.device)
         # q[:, :, 0, :] and out[:, 0] by strides (no views)
         qs_b, qs_h, os_b, os_h = query.stride(0), query.stride(1), out.stride(0), out.stride(2)
-        if st.pending is not None:
-            k, v = st.pending
-            st.pending = None
-            check(L.skv_decode_attention_append(
-                C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
-                query.data_ptr(), qs_b, qs_h, out.data_ptr(), os_b, os_h, float(scaling),
-                side.scores.data_ptr(), st.scores_cap, ws.data_ptr(), ws.numel(), _stream(st.device)),
-                "skv_decode_attention_append")
-        else:
-            check(L.skv_decode_attention(
-                C.byref(d), st.T, st.tier_pages, query.data_ptr(), qs_b, qs_h, out.data_ptr(), os_b,
-                os_h, float(scaling), side.scores.data_ptr(), st.scores_cap, ws.data_ptr(), ws.numel(),
-                _stream(st.device)), "skv_decode_attention")
+        with _on(st.device):
+            if st.pending is not None:
+                k, v = st.pending
+                st.pending = None
+                check(L.skv_decode_attention_append(
+                    C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                    query.data_ptr(), qs_b, qs_h, out.data_ptr(), os_b, os_h, float(scaling),
+                    side.scores.data_ptr(), st.scores_cap, ws.data_ptr(), ws.numel(), _stream(st.device)),
+                    "skv_decode_attention_append")
+            else:
+                check(L.skv_decode_attention(
+                    C.byref(d), st.T, st.tier_pages, query.data_ptr(), qs_b, qs_h, out.data_ptr(), os_b,
+                    os_h, float(scaling), side.scores.data_ptr(), st.scores_cap, ws.data_ptr(), ws.numel(),
+                    _stream(st.device)), "skv_decode_attention")
         self._note_windows(st)
         return out
 
@@ -550,10 +571,11 @@ class WindowedCache(_HFCacheBase):
         L = lib()
         nbytes = L.skv_prefill_workspace_size(C.byref(d), P)
         ws = self._workspace(nbytes, st.device)
-        check(L.skv_prefill_attention(C.byref(d), P, q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                      out.data_ptr(), float(scaling), side.scores.data_ptr(),
-                                      st.scores_cap, ws.data_ptr(), ws.numel(), _stream(st.device)),
-              "skv_prefill_attention")
+        with _on(st.device):
+            check(L.skv_prefill_attention(C.byref(d), P, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                          out.data_ptr(), float(scaling), side.scores.data_ptr(),
+                                          st.scores_cap, ws.data_ptr(), ws.numel(), _stream(st.device)),
+                  "skv_prefill_attention")
         st.has_scores = False
         self._note_windows(st)
         return out

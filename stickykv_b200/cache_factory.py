@@ -3,8 +3,8 @@
 ``get_cache_classes("b200")`` returns ``(WindowedCache, WindowedCacheConfig,
 install_score_hooks)`` of this package.  The reference's own backends
 (``"flash_attn"``, ``"eager"``) are not provided here: this package only
-replaces the hot path.  A reference checkout can add one branch to its
-factory that returns this trio.
+replaces the hot path.  A reference checkout adds one branch to its
+``get_cache_classes`` that imports this package and returns this trio.
 """
 
 from __future__ import annotations

@@ -174,8 +174,13 @@ static bool decode_kernel_exists(const skv_layer_desc* L, int32_t T) {
   return G >= 1 && G <= 8;
 }
 
-static int check_decode(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,
-                        float* scores, int32_t scores_cap, void* ws, size_t ws_bytes) {
+}  // extern "C"
+
+namespace skv {
+// Every check of a decode call except those of its workspace (shared with
+// the allocation-free entry point, which has no workspace argument).
+int decode_precheck(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,
+                    float* scores, int32_t scores_cap) {
   int rc = check_layer(L);
   if (rc) return rc;
   if (T > 0 && !decode_kernel_exists(L, T)) return SKV_ERR_UNSUPPORTED;
@@ -184,6 +189,16 @@ static int check_decode(const skv_layer_desc* L, int32_t T, int32_t tier_pages, 
   const Geometry g = geometry(L, T, tier_pages);
   if (scores && scores_cap < g.num_windows()) return SKV_ERR_CAPACITY;
   if (tier_pages > 0 && L->rope_positions < L->num_sink + tier_pages * kPageTokens) return SKV_ERR_CAPACITY;
+  return SKV_OK;
+}
+}  // namespace skv
+
+extern "C" {
+
+static int check_decode(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,
+                        float* scores, int32_t scores_cap, void* ws, size_t ws_bytes) {
+  const int rc = decode_precheck(L, T, tier_pages, q, out, scores, scores_cap);
+  if (rc) return rc;
   if (!ws || ws_bytes < skv_decode_workspace_size(L, T)) return SKV_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return SKV_ERR_MISALIGNED;
   return SKV_OK;

@@ -877,6 +877,13 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
   }
 }
 
+// Most splits a cache of U units can get (bounds the partials' workspace):
+// at least one full tile per split, at most kMaxUnitsPerSplit units each.
+int max_splits(int U) {
+  const int n = max(max(1, U / 16), ceil_div(U, kMaxUnitsPerSplit));
+  return n < kMaxSplits ? n : kMaxSplits;
+}
+
 template <int D>
 void plan_splits(MmaParams& p) {
   // Ranges hold equal estimated cost (the per-tile costs of the kernel's
@@ -911,7 +918,8 @@ void plan_splits(MmaParams& p) {
     ++k;
   }
   p.n_split = k - 1;
-  if (p.bnd[p.n_split] != p.U) {  // caps left units over: fall back to equal unit counts
+  if (p.bnd[p.n_split] != p.U || p.n_split > max_splits(p.U)) {
+    // caps left units over: fall back to equal unit counts
     n = max(ceil_div(p.U, kMaxUnitsPerSplit), min(n, kMaxSplits));
     const int per = (ceil_div(p.U, n) + 1) & ~1;
     p.n_split = ceil_div(p.U, per);
@@ -957,7 +965,8 @@ MmaWs mma_ws(const skv_layer_desc* L, int T) {
   MmaWs w{};
   const int W = T > L->num_sink ? (T - L->num_sink + kPageTokens - 1) / kPageTokens : 0;  // units
   const int Hv = head_groups(L);
-  w.part = align_up((size_t)L->batch * Hv * kMaxSplits * 4 * (L->head_dim + 2) * 4, 256);
+  const int NS = (min(T, L->num_sink) + kPageTokens - 1) / kPageTokens;
+  w.part = align_up((size_t)L->batch * Hv * max_splits(W + NS) * 4 * (L->head_dim + 2) * 4, 256);
   w.mass = align_up((size_t)L->batch * Hv * 4 * (W > 0 ? W : 1) * 4, 256);
   w.total = w.part + w.mass;
   return w;

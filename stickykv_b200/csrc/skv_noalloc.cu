@@ -9,6 +9,11 @@
 // library reserves SKV_NOALLOC_SCRATCH_BYTES for it until the process exits.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[SKV_NOALLOC_SCRATCH_BYTES];
 
+namespace skv {
+int decode_precheck(const skv_layer_desc* L, int32_t T, int32_t tier_pages, const void* q, void* out,
+                    float* scores, int32_t scores_cap);
+}
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -40,8 +45,11 @@ extern "C" int skv_decode_attention_noalloc(const skv_layer_desc* layer, int32_t
     skv::set_cuda_error(g_scratch_err[dev]);
     return SKV_ERR_CUDA;
   }
+  // the same argument checks, in the same order, as skv_decode_attention,
+  // so both entry points return the same status for the same bad input
+  const int rc = skv::decode_precheck(layer, seq_len, tier_pages, q, out, window_scores, scores_capacity);
+  if (rc != SKV_OK) return rc;
   const size_t need = skv_decode_workspace_size(layer, seq_len);
-  if (need == 0) return SKV_ERR_INVALID_ARG;
   if (need > (size_t)SKV_NOALLOC_SCRATCH_BYTES) return SKV_ERR_CAPACITY;
   // Every scratch byte the decode kernels read is written earlier in the same
   // call, so nothing needs clearing between calls.

@@ -89,6 +89,12 @@ def stickykv_attention(module: nn.Module, query: torch.Tensor, key: torch.Tensor
     if cache is None:
         raise RuntimeError(
             "stickykv_b200 attention needs install_score_hooks(model, cache, config) first")
+    if attention_mask is not None:
+        # the mask function registered with this implementation returns None
+        # for every unpadded causal batch, so a mask here means padding
+        raise NotImplementedError(
+            "stickykv_b200 attends over every cached token of a row: padded batches "
+            "(an attention_mask with masked positions) are not supported")
     layer = module.layer_idx
     if scaling is None:
         scaling = getattr(module, "scaling", query.shape[-1] ** -0.5)
@@ -102,7 +108,12 @@ def stickykv_attention(module: nn.Module, query: torch.Tensor, key: torch.Tensor
 
 def _register_attention() -> None:
     from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
     AttentionInterface.register(ATTN_IMPLEMENTATION, stickykv_attention)
+    # transformers builds no mask for an implementation without a mask
+    # function; the sdpa one skips the mask (None) for unpadded causal batches
+    # and materialises it when a row is padded, which the attention refuses
+    AttentionMaskInterface.register(ATTN_IMPLEMENTATION, sdpa_mask)
 
 
 def install_score_hooks(model: nn.Module, cache: Any, config: Any) -> HookHandles:

@@ -119,3 +119,17 @@ def fp_parts(cache, layer=0):
     k = to_np(side.k)
     v = to_np(side.v)
     return k[:, :, :s], v[:, :, :s], k[:, :, s_pad:s_pad + rest], v[:, :, s_pad:s_pad + rest]
+
+
+def tier_codes_all(cache, layer=0):
+    """Vectorised :func:`tier_codes` over every row and kv head: the logical
+    int4 tier (pages in table order) as oracle-shaped arrays
+    (kc, ks, kz, vc, vs, vz), each [B, Hkv, pages*8, ...]."""
+    st = cache._states[layer]
+    side = st.sides[st.cur]
+    n = st.tier_pages
+    pages = st.pages.cpu().numpy()
+    table = side.table[:, :n].cpu().numpy().astype(np.int64)
+    logical = np.take_along_axis(pages, table[:, None, :, None], axis=2)   # [B, H, n, PB]
+    parts = O.unpack_pages(logical, st.D)
+    return tuple(a.reshape(a.shape[:2] + (n * 8,) + a.shape[4:]) for a in parts)

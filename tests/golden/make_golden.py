@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout is available:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <path of the reference checkout>
 
 It imports the reference read-only (``sys.path``) and writes small ``.npz`` /
 ``.json`` fixtures next to this script.  The fixtures are committed; nothing at
@@ -293,7 +293,7 @@ def gen_cfg1_e2e(ref_eager):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of the reference checkout (imported read-only)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from modules.windowed_cache import scorer

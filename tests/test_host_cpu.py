@@ -197,6 +197,27 @@ def test_hook_handles_idempotent_and_null_telemetry():
     assert t.get_records(0) == []
 
 
+def test_padded_batches_are_refused():
+    """transformers builds no mask for an unknown attention implementation;
+    this package registers the sdpa mask function with its own, which skips
+    the mask for unpadded causal batches, so a mask reaching the attention
+    means padding, and the attention refuses it."""
+    from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS
+    from stickykv_b200.hooks import ATTN_IMPLEMENTATION, _register_attention, stickykv_attention
+    _register_attention()
+    assert ATTN_IMPLEMENTATION in ALL_MASK_ATTENTION_FUNCTIONS
+
+    class Attn(torch.nn.Module):
+        layer_idx = 0
+        _skv_cache = object()
+
+    q = torch.zeros(2, 4, 6, 16)
+    k = torch.zeros(2, 2, 6, 16)
+    mask = torch.ones(2, 1, 6, 6, dtype=torch.bool)
+    with pytest.raises(NotImplementedError, match="padded"):
+        stickykv_attention(Attn(), q, k, k, mask)
+
+
 def _install(seq_len):
     captured = {}
 

@@ -262,3 +262,55 @@ def test_page_frame_rotation_is_consistent():
         lhs = q @ k_post[0, i]
         rhs = O.rotate_query_to_page(q, P, cos, sin) @ kf[0, i]
         assert abs(lhs - rhs) < 1e-4 * (1 + abs(lhs))
+
+
+def test_vectorised_page_unpack_equals_scalar_unpack():
+    rng = np.random.default_rng(5)
+    for D in (64, 128):
+        pages = []
+        for _ in range(6):
+            kc = rng.integers(0, 16, (8, D)).astype(np.uint8)
+            vc = rng.integers(0, 16, (8, D)).astype(np.uint8)
+            sc = [rng.standard_normal((8, D // 32)).astype(np.float16) for _ in range(4)]
+            pages.append(O.pack_page(kc, sc[0], sc[1], vc, sc[2], sc[3]))
+        arr = np.stack(pages).reshape(2, 3, -1)
+        got = O.unpack_pages(arr, D)
+        for i in range(6):
+            want = O.unpack_page(pages[i], D)
+            for a, b in zip(got, want):
+                np.testing.assert_array_equal(a.reshape((6,) + a.shape[2:])[i], b)
+
+
+def test_grouped_tiered_attention_equals_per_page_loop():
+    rng = np.random.default_rng(6)
+    B, Hkv, G, D, s, nt, nr = 2, 2, 4, 64, 4, 48, 37
+    inv = (1.0 / (500000.0 ** (np.arange(0, D, 2) / D))).astype(np.float32)
+    cos, sin = O.rope_tables(inv, 200)
+    f = lambda *sh: rng.standard_normal(sh).astype(np.float32)
+    args = (f(B, Hkv * G, D), f(B, Hkv, s, D), f(B, Hkv, s, D), f(B, Hkv, nt, D), f(B, Hkv, nt, D),
+            f(B, Hkv, nr, D), f(B, Hkv, nr, D), s, 8, D ** -0.5, cos, sin)
+    o1, m1 = O.tiered_decode_attention(*args)
+    o2, m2 = O.tiered_decode_attention_grouped(*args)
+    np.testing.assert_allclose(o2, o1, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(m2, m1, rtol=1e-5, atol=1e-7)
+
+
+def test_tie_fixture_puts_equal_means_across_the_threshold():
+    """The tie-heavy scores of the GPU tie test (one of a few dyadic levels
+    per window, equal across heads) do put several equal head means at the
+    top-k threshold, and the oracle keeps the lowest-index ones."""
+    rng = np.random.default_rng(21)
+    B, Hq, W, k, loc = 4, 8, 150, 37, 10
+    per_w = rng.choice(np.asarray((0.25, 0.5, 0.75), np.float32), size=(B, W))
+    sc = np.ascontiguousarray(np.broadcast_to(per_w[:, None, :], (B, Hq, W)))
+    mean = O.head_mean(sc)
+    np.testing.assert_array_equal(mean, per_w)
+    ret = O.retain_window_indices(sc, k, loc)
+    for b in range(B):
+        ev = mean[b, : W - loc]
+        kth = np.sort(ev)[::-1][k - 1]
+        tied = np.flatnonzero(ev == kth)
+        n_above = int((ev > kth).sum())
+        assert tied.size > k - n_above  # more tied windows than places left
+        kept_tied = [w for w in ret[b, :k] if ev[w] == kth]
+        np.testing.assert_array_equal(kept_tied, tied[: k - n_above])

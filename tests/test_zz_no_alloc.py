@@ -84,3 +84,47 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
                                           q.data_ptr(), q.stride(0), q.stride(1), C.c_float(0.125),
                                           None, 0, torch.cuda.current_stream().cuda_stream)
     assert rc == 4  # SKV_ERR_CAPACITY
+
+
+def test_noalloc_after_a_larger_call_matches_a_nan_filled_workspace():
+    """The shared scratch keeps whatever the previous call left there: a call
+    with more rows, splits and windows, then a smaller one whose result must
+    equal the workspace entry point's given a workspace full of NaN (so any
+    read of a byte the call did not write would show)."""
+    from stickykv_b200 import _lib
+    lib = _lib.lib()
+    g = torch.Generator().manual_seed(12)
+    D, G, Hkv = 64, 4, 2
+    Hq = Hkv * G
+    results = []
+    for B, P in ((6, 3001), (2, 517)):
+        cos, sin = rope_tables(5e5, D, P + 64)
+        cache = make_cache("f16", B, Hkv, Hq, D, P, 16, cos, sin, tier=True)
+        cache.update(rand((B, Hkv, P, D), "f16", g).cuda(), rand((B, Hkv, P, D), "f16", g).cuda(), 0)
+        st = cache._states[0]
+        W = -(-(P - 4) // 8)
+        st.sides[st.cur].scores[:, :, :W] = torch.rand(B, Hq, W, generator=g).cuda()
+        st.has_scores, st.W, st.next_window_id = True, W, W
+        for _ in range(9):
+            k1 = rand((B, Hkv, 1, D), "f16", g).cuda()
+            cache.update(k1, k1.clone(), 0)
+        if st.pending is not None:
+            cache._flush(st)
+        desc = cache._desc(st, st.sides[st.cur])
+        q = rand((B, Hq, D), "f16", g, scale=2.0).cuda()
+        cap = st.scores_cap
+        out_na = torch.full((B, Hq, D), float("nan"), dtype=q.dtype, device="cuda")
+        sc_na = torch.zeros(B, Hq, cap, device="cuda")
+        assert _call(lib, lib.skv_decode_attention_noalloc, desc, st, q, out_na, sc_na) == 0, \
+            lib.skv_last_cuda_error()
+        nbytes = lib.skv_decode_workspace_size(C.byref(desc), st.T)
+        ws = torch.full((nbytes // 4,), float("nan"), device="cuda").view(torch.uint8)
+        out_ref = torch.empty_like(out_na)
+        sc_ref = torch.zeros_like(sc_na)
+        assert _call(lib, lib.skv_decode_attention, desc, st, q, out_ref, sc_ref, ws) == 0
+        torch.cuda.synchronize()
+        results.append((to_np(out_na), to_np(out_ref), to_np(sc_na), to_np(sc_ref)))
+    for i, (a, b, sa, sb) in enumerate(results):
+        assert np.isfinite(a).all() and np.isfinite(sa).all(), f"call {i}"
+        np.testing.assert_array_equal(a, b, err_msg=f"call {i}")
+        np.testing.assert_array_equal(sa, sb, err_msg=f"call {i}")
