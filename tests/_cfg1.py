@@ -57,3 +57,25 @@ def greedy(model, cache, ids: torch.Tensor, at=None, **fwd) -> Tuple[List[int], 
             top_v.append(v.cpu().numpy())
             inp = torch.tensor([[toks[-1]]], device=ids.device)
     return toks, np.stack(top_i), np.stack(top_v)
+
+
+def teacher_forced(model, cache, ids: torch.Tensor, tokens, at=None, **fwd) -> Tuple[np.ndarray, np.ndarray]:
+    """Prefill then STEPS-1 one-token steps feeding ``tokens[step-1]`` (a fixed
+    sequence, so two implementations see the same inputs whatever their own
+    argmax).  Returns (top-k logit indices [STEPS, K], their logits [STEPS,
+    K]); with ``at`` the logits are read at those indices instead."""
+    top_i, top_v = [], []
+    inp = ids
+    with torch.no_grad():
+        for step in range(STEPS):
+            out = model(input_ids=inp, past_key_values=cache, use_cache=True, return_dict=True, **fwd)
+            lg = out.logits[0, -1].float()
+            v, i = torch.topk(lg, TOPK_LOGITS)
+            if at is not None:
+                i = torch.as_tensor(at[step], device=lg.device)
+                v = lg[i]
+            top_i.append(i.cpu().numpy())
+            top_v.append(v.cpu().numpy())
+            if step + 1 < STEPS:
+                inp = torch.tensor([[int(tokens[step])]], device=ids.device)
+    return np.stack(top_i), np.stack(top_v)

@@ -26,6 +26,9 @@ Fixtures:
                        top-64 logits per step, final per-layer window ids,
                        window scores, the last step's not yet accumulated
                        scores, and seq length)
+  cfg1_e2e_<dt>.npz    the same model cast to fp16 / bf16: teacher-forced on
+                       the fp32 tokens (logits, window ids, scores) and
+                       free-running greedy (tokens, top-2 margins)
 """
 
 from __future__ import annotations
@@ -291,6 +294,69 @@ def gen_cfg1_e2e(ref_eager):
     np.savez_compressed(os.path.join(HERE, "cfg1_e2e.npz"), **rec)
 
 
+def gen_cfg1_e2e_half(ref_eager):
+    """The cfg1 model cast to fp16 and to bf16 through the reference's eager
+    backend (same harness shim as :func:`gen_cfg1_e2e`; matmuls accumulate in
+    fp32, the softmax runs in fp32 and is cast to the model dtype, window
+    scores accumulate in the model dtype).  Two runs per dtype:
+    teacher-forced on the fp32 run's greedy tokens (top-64 logits per step,
+    final per-layer window ids, scores, the last step's pending scores, seq
+    length) and free-running greedy (tokens and the top-1/top-2 logit margin
+    of every step)."""
+    import transformers.models.llama.modeling_llama as LM
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("skv_cfg1", os.path.join(os.path.dirname(HERE), "_cfg1.py"))
+    C1 = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(C1)
+    fp32 = np.load(os.path.join(HERE, "cfg1_e2e.npz"))
+
+    class Shim(ref_eager.WindowedCache):
+        layers = []
+        is_compileable = False
+
+        def get_mask_sizes(self, q_len, layer_idx=0):
+            q = int(q_len.shape[0]) if torch.is_tensor(q_len) else int(q_len)
+            return self.get_seq_length(layer_idx) + q, 0
+
+    eager = LM.eager_attention_forward
+
+    def eager_trimmed(module, q, k, v, mask, *a, **kw):
+        if mask is not None:
+            mask = mask[..., : k.shape[-2]]
+        return eager(module, q, k, v, mask, *a, **kw)
+
+    LM.eager_attention_forward = eager_trimmed
+    try:
+        for name, dt in (("f16", torch.float16), ("bf16", torch.bfloat16)):
+            rec = {"tf_tokens": fp32["tokens"]}
+            for mode in ("tf", "greedy"):
+                model = C1.build_model().to(dt)
+                wcfg = ref_eager.WindowedCacheConfig(window_size=C1.WINDOW, num_sink_tokens=C1.SINKS,
+                                                     local_window_size=C1.LOCAL, cache_budget=C1.BUDGET)
+                cache = Shim(config=wcfg, prefill_len=C1.PROMPT_LEN, model_config=model.config,
+                             kv_dtype=dt, rope_module=model.model.rotary_emb, num_layers=2,
+                             max_tokens=C1.STEPS)
+                handles = ref_eager.install_score_hooks(model, cache, wcfg)
+                if mode == "tf":
+                    top_i, top_v = C1.teacher_forced(model, cache, C1.prompt(), fp32["tokens"],
+                                                     output_attentions=True)
+                    rec.update(tf_top_i=top_i.astype(np.int64), tf_top_v=top_v.astype(np.float32),
+                               tf_seq_len=np.array(cache.get_seq_length(0)))
+                    for li in range(2):
+                        st = cache._states[li]
+                        rec[f"tf_ids_{li}"] = to_np(st.original_window_ids)
+                        rec[f"tf_scores_{li}"] = to_np(st.window_scores)
+                        rec[f"tf_pending_{li}"] = to_np(cache.cache_kwargs[li]["window_scores"])
+                else:
+                    toks, _, top_v = C1.greedy(model, cache, C1.prompt(), output_attentions=True)
+                    rec.update(greedy_tokens=np.array(toks, np.int64),
+                               greedy_margin=(top_v[:, 0] - top_v[:, 1]).astype(np.float32))
+                handles.remove()
+            np.savez_compressed(os.path.join(HERE, f"cfg1_e2e_{name}.npz"), **rec)
+    finally:
+        LM.eager_attention_forward = eager
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout (imported read-only)")
@@ -311,6 +377,7 @@ def main():
     gen_prefill_scores(scorer)
     import modules.windowed_eager_cache as ref_eager
     gen_cfg1_e2e(ref_eager)
+    gen_cfg1_e2e_half(ref_eager)
     print("golden fixtures written to", HERE)
 
 

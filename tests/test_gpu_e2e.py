@@ -49,11 +49,102 @@ def test_cfg1_greedy_generation_matches_reference():
     assert model.config._attn_implementation == "eager"  # restored by remove()
 
 
+HALF_TOL = {"f16": 2e-3, "bf16": 8e-3}  # max-abs logit tolerance per model dtype
+
+
+def _b200_cache(model, dtype, steps=C1.STEPS):
+    from stickykv_b200.cache_factory import get_cache_classes
+    Cache, Config, install = get_cache_classes("b200")
+    cfg = Config(window_size=C1.WINDOW, num_sink_tokens=C1.SINKS, local_window_size=C1.LOCAL,
+                 cache_budget=C1.BUDGET)
+    cache = Cache(cfg, C1.PROMPT_LEN, model.config, dtype, model.model.rotary_emb, 2, steps)
+    return cache, install(model, cache, cfg)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_cfg1_half_precision_matches_reference(dt):
+    """The cfg1 model cast to fp16 / bf16 against the reference's eager
+    backend in the same dtype (tests/golden/cfg1_e2e_<dt>.npz).
+
+    Teacher-forced on one fixed token sequence (so both runs see the same
+    inputs): logits at the reference's top-64 indices within max-abs 2e-3
+    (fp16) / 8e-3 (bf16) at all 50 steps; the kept windows (original ids) of
+    both layers and the final length bit-exact; window scores within the
+    rounding of the reference, which accumulates them in the model dtype
+    (this backend accumulates in fp32).
+
+    Free-running greedy: every token equal to the reference's own greedy
+    token.  At a step where the reference's top two logits are within the
+    tolerance of each other the two runs may legitimately pick different
+    tokens (the tie is below the numerical contract) and the sequences then
+    part; the comparison stops there.  Most such ties in this tiny random
+    model are exact ties of the rounded logits."""
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", f"cfg1_e2e_{dt}.npz"))
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    tol = HALF_TOL[dt]
+    model = C1.build_model().to(tdt).cuda()
+    cache, handles = _b200_cache(model, tdt)
+    try:
+        _, logits = C1.teacher_forced(model, cache, C1.prompt().cuda(), z["tf_tokens"], at=z["tf_top_i"])
+    finally:
+        handles.remove()
+    err = np.abs(logits - z["tf_top_v"]).max(axis=1)
+    assert err.max() <= tol, f"logits differ by {err.max():.2e} (step {int(err.argmax())})"
+    assert cache.get_seq_length(0) == int(z["tf_seq_len"])
+    for li in range(2):
+        st = cache._states[li]
+        np.testing.assert_array_equal(st.original_window_ids.cpu().numpy(), z[f"tf_ids_{li}"], err_msg=f"layer {li}")
+        want = z[f"tf_scores_{li}"].astype(np.float32).copy()
+        pend = z[f"tf_pending_{li}"]
+        want[..., : pend.shape[-1]] += pend[..., : want.shape[-1]]
+        # the reference adds each step's mass to a model-dtype accumulator: in
+        # bf16 an addend below half an ulp of the running sum (1/16 at 16)
+        # is rounded away, so its scores stall (fp16 keeps 3 more bits)
+        np.testing.assert_allclose(st.window_scores.float().cpu().numpy(), want,
+                                   rtol={"f16": 8 * tol, "bf16": 0.15}[dt], atol=1e-4)
+    # free-running greedy
+    model = C1.build_model().to(tdt).cuda()
+    cache, handles = _b200_cache(model, tdt)
+    try:
+        toks, _, _ = C1.greedy(model, cache, C1.prompt().cuda())
+    finally:
+        handles.remove()
+    ref = z["greedy_tokens"].tolist()
+    for i, (a, b) in enumerate(zip(toks, ref)):
+        if a != b:
+            assert z["greedy_margin"][i] <= tol, (
+                f"step {i}: token {a} vs the reference's {b} with a top-2 margin of "
+                f"{z['greedy_margin'][i]:.2e} (above the {tol} tolerance)")
+            break
+
+
+def test_generate_drop_in_matches_the_reference_run():
+    """The README usage, model.generate(input_ids, past_key_values=cache,
+    max_new_tokens=50), through get_cache_classes("b200"): the same 50 greedy
+    tokens, kept windows and final length as the reference's eager backend
+    driven step by step (tests/golden/cfg1_e2e.npz)."""
+    z = np.load(GOLDEN)
+    model = C1.build_model().cuda()
+    cache, handles = _b200_cache(model, torch.float32)
+    ids = C1.prompt().cuda()
+    try:
+        with torch.no_grad():
+            out = model.generate(ids, past_key_values=cache, max_new_tokens=C1.STEPS, do_sample=False,
+                                 min_new_tokens=C1.STEPS, pad_token_id=0)
+    finally:
+        handles.remove()
+    assert out[0, C1.PROMPT_LEN:].tolist() == z["tokens"].tolist()
+    assert cache.get_seq_length(0) == int(z["seq_len"])
+    for li in range(2):
+        np.testing.assert_array_equal(cache._states[li].original_window_ids.cpu().numpy(), z[f"ids_{li}"])
+
+
 def test_qwen2_gqa7_matches_transformers_attention_without_eviction():
     """A 2-layer Qwen2-shaped fp16 model with 14 query and 2 kv heads (GQA 7,
     head_dim 64, the tensor-core decode's head groups of 4 + 3) through this
     package's hooks, with a budget that never evicts: every step's logits
-    match transformers' own cache and eager attention on the same tokens."""
+    match transformers' own cache and eager attention on the same tokens
+    within the fp16 contract (2e-3 max-abs)."""
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
     from stickykv_b200.cache_factory import get_cache_classes
@@ -88,5 +179,5 @@ def test_qwen2_gqa7_matches_transformers_attention_without_eviction():
     finally:
         handles.remove()
     for t, (a, b) in enumerate(zip(got, ref)):
-        torch.testing.assert_close(a, b, atol=2e-2, rtol=0, msg=f"step {t}")
+        torch.testing.assert_close(a, b, atol=HALF_TOL["f16"], rtol=0, msg=f"step {t}")
     assert cache.get_seq_length(0) == P + steps - 1
