@@ -11,9 +11,14 @@ larger than the 126 MB L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs as torchrun ranks, one GPU each, every rank with its own batch of
-16 rows (weak scaling, no collective on the data path); the reported value
-is the sum over ranks of rows decoded per second, timed as the max over ranks.
+The timed steps replay one captured CUDA graph per step (the host code of a
+step runs once, at capture); `e2e` runs the same steps through the Python API
+with host buffers.  N > 1 runs as torchrun ranks, one GPU each, the 16 rows
+partitioned over the ranks (strong scaling, no collective on the attention
+path); the reported value is the 16 rows decoded per second, timed as the max
+over ranks.  The default line also carries `model_e2e`: the Llama-3.2-1B
+shaped decoder of run_e2e with its global batch of 32 rows partitioned over
+the ranks (skip with --no-model).
 """
 
 from __future__ import annotations
@@ -101,22 +106,27 @@ def max_over_ranks(values, dev, world):
 
 
 def rows_per_rank(batch, world):
-    """Rows of a global batch each rank decodes (batch shards; no row is shared)."""
-    return max(1, batch // world)
+    """Rows of the global batch each rank decodes: the batch is partitioned
+    across the ranks (rows never interact, so no collective is needed on the
+    attention path)."""
+    if batch % world:
+        raise ValueError(f"batch {batch} does not split evenly over {world} ranks")
+    return batch // world
 
 
-def gather_tokens(nxt, gathered, world):
-    """All-gather every rank's next tokens [rows, 1] into `gathered`
-    [world * rows, 1] in rank order (the end-to-end run's one collective)."""
+def gather_logits(logits, gathered, world):
+    """All-gather every rank's last-position logits [rows, vocab] into
+    `gathered` [world * rows, vocab] in rank order over NCCL (the end-to-end
+    run's one collective)."""
     import torch.distributed as dist
     if world > 1:
-        dist.all_gather_into_tensor(gathered, nxt)
-    return gathered if world > 1 else nxt
+        dist.all_gather_into_tensor(gathered, logits)
+        return gathered
+    return logits
 
 
-def build_steady_cache(dev, seed, tier=True):
+def build_steady_cache(dev, seed, rows=B, tier=True):
     """A layer cache at 32k context after its first eviction (steady state)."""
-    import numpy as np
     import torch
 
     from stickykv_b200 import WindowedCache, WindowedCacheConfig
@@ -139,18 +149,18 @@ def build_steady_cache(dev, seed, tier=True):
                               cache_budget=BUDGET, int4_tier=tier)
     cache = WindowedCache(cfg, CTX, MC(), torch.float16, RoPE(500000.0), num_layers=1, max_tokens=0)
     g = torch.Generator(device=dev).manual_seed(seed)
-    k = torch.randn(B, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
-    v = torch.randn(B, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
+    k = torch.randn(rows, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
+    v = torch.randn(rows, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
     cache.update(k, v, 0)
     del k, v
     st = cache._states[0]
     W = math.ceil((CTX - SINKS) / WS)
-    st.sides[st.cur].scores[:, :, :W] = torch.rand(B, HQ, W, device=dev, generator=g)
+    st.sides[st.cur].scores[:, :, :W] = torch.rand(rows, HQ, W, device=dev, generator=g)
     st.has_scores, st.W, st.next_window_id = True, W, W
     # 9 decode steps: the 9th (generation step 8) runs the first eviction
-    q = torch.randn(B, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
+    q = torch.randn(rows, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
     for _ in range(WS + 1):
-        kn = torch.randn(B, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+        kn = torch.randn(rows, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
         cache.update(kn, kn.clone(), 0)
         cache.decode_attention(0, q, D ** -0.5)
     torch.cuda.synchronize(dev)
@@ -165,7 +175,63 @@ def algorithmic_bytes(cache):
     st = cache._states[0]
     n_fp = st.T - st.tier_pages * 8
     per_int4 = _lib.page_bytes(D) / 8
-    return B * HKV * (n_fp * 2 * D * 2 + st.tier_pages * 8 * per_int4) + B * HQ * D * 2 * 2
+    return st.B * HKV * (n_fp * 2 * D * 2 + st.tier_pages * 8 * per_int4) + st.B * HQ * D * 2 * 2
+
+
+def evict_algorithmic_bytes(cache):
+    """HBM bytes of the eviction the cache's next evicting step runs (with
+    the length it will have then): the accumulated scores read and the
+    retained ones written, every fp token that stays fp read and written
+    (K and V: compaction and re-rotation), the fp windows that may enter the
+    tier read (all candidates, an upper bound) and their int4 pages written,
+    ids and page tables read and written."""
+    from stickykv_b200 import _lib
+    st = cache._states[0]
+    r = cache.resolved
+    n = (WS - cache._generation_step[0] % WS) % WS  # updates before the evicting one
+    T = st.T + n + 1                                 # its length after its append
+    W = math.ceil((T - 1 - SINKS) / WS)              # windows its scores cover
+    plan = _lib.evict_plan(T, W, SINKS, WS, r.top_k_windows, cache.local_windows, cache.tier)
+    n_tw_old = st.tier_pages * 8 // WS
+    n_cand = plan.evictable_windows - n_tw_old
+    fp_kept = plan.seq_len_new - plan.tier_pages_new * 8
+    rows = st.B
+    kv = rows * HKV * D * 2 * 2                                   # K+V bytes per token, all kv heads
+    return (rows * HQ * W * 4 + rows * HQ * plan.retained_windows * 4 + rows * (W + plan.retained_windows) * 8
+            + fp_kept * kv * 2 + n_cand * WS * kv + rows * HKV * n_cand * (WS // 8) * _lib.page_bytes(D)
+            + 2 * rows * st.page_cap * 4)
+
+
+class StepGraphs:
+    """One CUDA graph per step of a 16-step cycle (two evictions apart, so
+    the ping-pong stores are back where they started): in steady state every
+    step of the cycle launches the same kernels with the same lengths, so the
+    graph of phase j replays step j of every cycle with no host work but one
+    graph launch.  Capture runs the host code of the 16 steps once (advancing
+    its counters by one cycle) without device work; replaying the 16 graphs
+    in order then performs those steps on the device."""
+
+    def __init__(self, step, cycle, stream):
+        import torch
+        self.graphs = []
+        self.cycle = cycle
+        self.pos = 0
+        for j in range(cycle):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(j)
+            self.graphs.append(g)
+
+    def replay(self, n):
+        for _ in range(n):
+            self.graphs[self.pos].replay()
+            self.pos = (self.pos + 1) % self.cycle
+
+    def finish_cycle(self):
+        """Replay up to the end of the current cycle (device and host state
+        agree again)."""
+        if self.pos:
+            self.replay(self.cycle - self.pos)
 
 
 def run_ours(args, rank, world, dev):
@@ -173,73 +239,106 @@ def run_ours(args, rank, world, dev):
     import torch
     import torch.distributed as dist
 
-    cache = build_steady_cache(dev, seed=1 + rank, tier=not args.no_tier)
+    rows = rows_per_rank(B, world)
+    cache = build_steady_cache(dev, seed=1 + rank, rows=rows, tier=not args.no_tier)
     st = cache._states[0]
     g = torch.Generator(device=dev).manual_seed(100 + rank)
-    nq = 64
-    qs = torch.randn(nq, B, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
-    ks = torch.randn(nq, B, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
-    vs = torch.randn(nq, B, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
-    stream = torch.cuda.current_stream(dev)
+    cycle = 2 * WS
+    qs = torch.randn(cycle, rows, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
+    ks = torch.randn(cycle, rows, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+    vs = torch.randn(cycle, rows, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+    stream = torch.cuda.Stream(dev)
     scale = D ** -0.5
 
-    def step(i, ev=None):
-        j = i % nq
+    def step(j):
         cache.update(ks[j], vs[j], 0)
-        if ev is not None:
-            ev[0].record(stream)
-        out = cache.decode_attention(0, qs[j], scale)
-        if ev is not None:
-            ev[1].record(stream)
-        return out
+        return cache.decode_attention(0, qs[j], scale)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize(dev)
-    bytes_per_launch = algorithmic_bytes(cache)
-    attn_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(args.steps)]
-    step0 = cache._generation_step[0]
-    sampler = ClockSampler(dev.index if dev.index is not None else 0)
-    sampler.start()
-    time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(args.steps):
-        step(args.warmup + i, attn_events[i])
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop()
-    ms = t0.elapsed_time(t1)
-    attn_ms = [a.elapsed_time(b) for a, b in attn_events]
-    n_evict = sum(1 for s in range(step0, step0 + args.steps) if s > 0 and s % WS == 0)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i % cycle)
+        # align to the start of a cycle, then one host-driven cycle with
+        # events around the evicting updates (and the host time per step)
+        while cache._generation_step[0] % cycle:
+            step(cache._generation_step[0] % cycle)
+        evict_bytes = evict_algorithmic_bytes(cache)
+        ev = []
+        t_host = time.perf_counter()
+        for j in range(cycle):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            gs = cache._generation_step[0]  # update() at generation step gs evicts when gs % WS == 0
+            e[0].record(stream)
+            cache.update(ks[j], vs[j], 0)
+            e[1].record(stream)
+            cache.decode_attention(0, qs[j], scale)
+            ev.append((e, gs > 0 and gs % WS == 0))
+        host_us = (time.perf_counter() - t_host) * 1e6 / cycle
+        torch.cuda.synchronize(dev)
+        evict_ms = [a[0].elapsed_time(a[1]) for a, is_ev in ev if is_ev]
+        # decode launches alone (decode + merge), back to back in one graph: no
+        # host gaps, the cache unchanged between calls
+        bytes_per_launch = algorithmic_bytes(cache)
+        n_dec = 20
+        gd = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gd, stream=stream):
+            for _ in range(n_dec):
+                cache.decode_attention(0, qs[0], scale)
+        for _ in range(2):
+            gd.replay()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for _ in range(5):
+            gd.replay()
+        d1.record(stream)
+        torch.cuda.synchronize(dev)
+        attn_ms = d0.elapsed_time(d1) / (5 * n_dec)
+        # the timed steps: graph replays (host-launch gaps removed)
+        graphs = StepGraphs(step, cycle, stream)
+        graphs.replay(cycle)  # one untimed cycle on the device
+        torch.cuda.synchronize(dev)
+        n_evict = sum(1 for i in range(args.steps) if i % WS == 0)  # phases 0 and 8 evict
+        sampler = ClockSampler(dev.index if dev.index is not None else 0)
+        sampler.start()
+        time.sleep(0.3)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        graphs.replay(args.steps)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop()
+        ms = t0.elapsed_time(t1)
+        graphs.finish_cycle()
+        torch.cuda.synchronize(dev)
+        del graphs, gd
+
     # e2e: the same step through the public API with host buffers inside the
     # timed region: one pinned H2D copy of this step's packed q|k|v at the
     # start of the step on the compute stream, one D2H copy of the attention
     # output on a copy stream (it overlaps the next step; the timed region
     # ends after the last copy)
-    nq_el, nk_el = B * HQ * D, B * HKV * D
-    hin = torch.randn(nq, nq_el + 2 * nk_el, generator=torch.Generator().manual_seed(7),
+    cstream = torch.cuda.current_stream(dev)
+    nq_el, nk_el = rows * HQ * D, rows * HKV * D
+    nbuf = cycle
+    hin = torch.randn(nbuf, nq_el + 2 * nk_el, generator=torch.Generator().manual_seed(7),
                       dtype=torch.float16).pin_memory()
-    hout = torch.empty(nq, B, 1, HQ, D, dtype=torch.float16).pin_memory()
+    hout = torch.empty(nbuf, rows, 1, HQ, D, dtype=torch.float16).pin_memory()
     din = torch.empty(nq_el + 2 * nk_el, device=dev, dtype=torch.float16)
-    dq = din[:nq_el].view(B, HQ, 1, D)
-    dk = din[nq_el:nq_el + nk_el].view(B, HKV, 1, D)
-    dv = din[nq_el + nk_el:].view(B, HKV, 1, D)
-
+    dq = din[:nq_el].view(rows, HQ, 1, D)
+    dk = din[nq_el:nq_el + nk_el].view(rows, HKV, 1, D)
+    dv = din[nq_el + nk_el:].view(rows, HKV, 1, D)
     copy_stream = torch.cuda.Stream(dev)
 
     def e2e_step(i):
-        j = i % nq
+        j = i % nbuf
         din.copy_(hin[j], non_blocking=True)
         cache.update(dk, dv, 0)
         out = cache.decode_attention(0, dq, scale)
-        copy_stream.wait_stream(stream)
+        copy_stream.wait_stream(cstream)
         with torch.cuda.stream(copy_stream):
             hout[j].copy_(out, non_blocking=True)
         out.record_stream(copy_stream)
@@ -250,20 +349,29 @@ def run_ours(args, rank, world, dev):
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record(cstream)
     for i in range(args.steps):
         e2e_step(i)
-    stream.wait_stream(copy_stream)
-    e1.record(stream)
+    cstream.wait_stream(copy_stream)
+    e1.record(cstream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
     h2d = din.numel() * 2
     d2h = hout[0].numel() * 2
-    ms, e2e_ms, attn_avg = max_over_ranks([ms, e2e_ms, float(np.mean(attn_ms))], dev, world)
+    evict_avg = float(np.mean(evict_ms)) if evict_ms else 0.0
+    ms, e2e_ms, attn_ms, evict_avg, host_us = max_over_ranks([ms, e2e_ms, attn_ms, evict_avg, host_us], dev,
+                                                             world)
+    del cache
+    torch.cuda.empty_cache()
+    model = None
+    if not args.no_model:
+        model = run_e2e(args, rank, world, dev)
     if rank != 0:
         return None
     peak, peak_kind = measured_hbm_peak()
-    achieved = bytes_per_launch / (attn_avg * 1e-3) / 1e9
+    achieved = bytes_per_launch / (attn_ms * 1e-3) / 1e9
+    step_bytes = (bytes_per_launch + evict_bytes / WS) * world
+    step_achieved = step_bytes / (ms / args.steps * 1e-3) / 1e9
     # every step: decode with its fused append, then the split merge; an
     # evicting step appends on its own and adds the select and apply kernels
     gpu_launches = args.steps * 2 + n_evict * 3
@@ -275,28 +383,42 @@ def run_ours(args, rank, world, dev):
         except (OSError, ValueError):
             traffic = None
     line = {
-        "metric": METRIC, "value": world * B * args.steps / (ms * 1e-3), "unit": UNIT,
+        "metric": METRIC, "value": B * args.steps / (ms * 1e-3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "f16 (int4 tier codes, fp32 accumulate)", "data": "synthetic N(0,1), seeded",
         "config": {"workload": "decode-attention + eviction step of one layer, 32k context, "
                                + ("all-fp16 retained cache" if args.no_tier else "int4 tier"),
-                   "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
-                   "cache_budget": BUDGET, "window_size": WS, "sinks": SINKS, "local": LOCAL,
+                   "global_batch": B, "rows_per_gpu": rows, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "context": CTX, "cache_budget": BUDGET, "window_size": WS, "sinks": SINKS, "local": LOCAL,
                    "retained_tokens": st.T, "int4_tokens": st.tier_pages * 8,
                    "evictions_in_timed_region": n_evict,
                    "l2": "working set per step > 126 MB L2; no flush",
-                   "parallelism": f"{world} independent batch shards (weak scaling)"},
+                   "launch": "each timed step replays that step's captured CUDA graph",
+                   "parallelism": f"batch partitioned over {world} GPUs ({rows} rows each), "
+                                  "no collective on the attention path"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                      "kernel": "decode attention (split + merge) per layer-step",
                      "algorithmic_bytes_per_launch": bytes_per_launch,
-                     "avg_launch_us": attn_avg * 1e3},
-        "e2e": {"value": world * B * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
+                     "avg_launch_us": attn_ms * 1e3},
+        "step_roofline": {"bound": "hbm", "achieved": step_achieved, "peak": peak * world, "unit": "GB/s",
+                          "frac": step_achieved / (peak * world),
+                          "algorithmic_bytes_per_step": step_bytes,
+                          "note": "decode launch + one eighth of an eviction per step, all GPUs, "
+                                  "over ms_per_step"},
+        "evict": {"algorithmic_bytes": evict_bytes, "avg_us": evict_avg * 1e3,
+                  "achieved_gbs": evict_bytes / (evict_avg * 1e-3) / 1e9 if evict_avg else None,
+                  "frac": evict_bytes / (evict_avg * 1e-3) / 1e9 / peak if evict_avg else None,
+                  "note": "append + select + apply of an evicting update(), events on the stream"},
+        "host_us_per_step": host_us,
+        "e2e": {"value": B * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": gpu_launches,
         "clocks": clocks,
     }
+    if model is not None:
+        line["model_e2e"] = model
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return line
@@ -354,7 +476,7 @@ def run_e2e(args, rank, world, dev):
     greedily decodes 256 tokens with the windowed cache (budget 0.40, int4
     tier).  The global batch of 32 rows is split across the ranks; decode
     tokens/s = rows x steps / decode time (max over ranks), prefill excluded.
-    At N > 1 the ranks all-gather each step's greedy tokens.  Also reported,
+    At N > 1 the ranks all-gather each step's logits.  Also reported,
     as the reference's perf runner does: time to first token (the prefill
     forward), time per output token and peak device memory; `--e2e-budget`
     sets the cache budget (0.10 / 0.25 / 0.50 in the reference's sweep)."""
@@ -401,15 +523,16 @@ def run_e2e(args, rank, world, dev):
         if world > 1:
             dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        # every step the ranks gather the batch's next tokens (NCCL over NVLink),
-        # the only collective of the run; each rank keeps decoding its own rows
-        gathered = torch.empty(world * rows, 1, dtype=torch.long, device=dev) if world > 1 else None
+        # every step the ranks all-gather the batch's last-position logits
+        # (NCCL over NVLink), the only collective of the run; each rank keeps
+        # decoding its own rows from its slice of the gathered logits
+        gathered = (torch.empty(world * rows, c["vocab"], dtype=torch.bfloat16, device=dev)
+                    if world > 1 else None)
         t0.record(stream)
         for _ in range(c["decode"] - 1):
             out = model(input_ids=nxt, past_key_values=cache, use_cache=True, logits_to_keep=1)
-            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
-            if gathered is not None:
-                gather_tokens(nxt, gathered, world)
+            logits = gather_logits(out.logits[:, -1].contiguous(), gathered, world)
+            nxt = logits[rank * rows:(rank + 1) * rows].argmax(-1, keepdim=True)
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
@@ -486,7 +609,7 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic N(0,1), seeded",
         "config": {"workload": "decode-attention + eviction step of one layer, 32k context",
-                   "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
+                   "global_batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
                    "sample_rows": 1, "note": "reference CPU path (numpy restatement), all-fp16 tiers"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"1 of {B} rows per step, {args.steps} timed steps"},
@@ -597,6 +720,8 @@ def main():
     ap.add_argument("--e2e-prompt", type=int, default=0)
     ap.add_argument("--e2e-decode", type=int, default=0)
     ap.add_argument("--e2e-budget", type=float, default=0.0)
+    ap.add_argument("--no-model", action="store_true",
+                    help="leave the Llama-3.2-1B-shaped model run out of the default line")
     ap.add_argument("--no-tier", action="store_true",
                     help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
     ap.add_argument("--tile-profile", action="store_true",

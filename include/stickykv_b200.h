@@ -121,7 +121,14 @@ typedef struct skv_evict_args {
   int32_t* retained_out;      /* optional [batch][scores_capacity] window idx */
   int64_t next_window_id;     /* original id of the next window to appear; the
                                  slots after the retained windows are seeded
-                                 with next_window_id, next_window_id+1, ... */
+                                 with next_window_id, next_window_id+1, ...
+                                 With num_windows > 0 the kernel takes it from
+                                 the device instead (one past ids_src of the
+                                 newest window, which equals it whenever ids
+                                 grow by one per new window, as the cache
+                                 keeps them), so a captured launch stays
+                                 valid on replay; this value serves
+                                 num_windows == 0. */
 } skv_evict_args;
 
 int skv_abi_version(void);

@@ -395,8 +395,12 @@ __device__ void gather_block(const EvictParams& p, const ApplyGrid& a, int bid) 
 #pragma unroll 8
   for (int h = 0; h < p.Hq; ++h)
     dst[(int64_t)h * p.scores_cap + j] = r >= 0 ? src[(int64_t)h * p.scores_cap + r] : 0.f;
+  // the next window's original id is one past the newest window's (ids
+  // grow by one per new window, cache.py:180-213); reading it here rather
+  // than from the host keeps a captured launch valid when replayed
+  const int64_t next_id = p.W > 0 ? p.ids_src[(int64_t)b * p.scores_cap + p.W - 1] + 1 : p.next_window_id;
   p.ids_dst[(int64_t)b * p.scores_cap + j] =
-      r >= 0 ? p.ids_src[(int64_t)b * p.scores_cap + r] : p.next_window_id + (j - p.R);
+      r >= 0 ? p.ids_src[(int64_t)b * p.scores_cap + r] : next_id + (j - p.R);
 }
 
 // fp tokens that stay fp, copied into the destination store with their keys

@@ -1,8 +1,9 @@
 """The multi-rank (N > 1) host path on CPU: world-size-2 `gloo` process
 groups stand in for the NCCL ranks of `torchrun ... bench.py --gpus 2`.
 
-Covered: the max-over-ranks reduction of timings, the batch sharding of the
-end-to-end run, the rank-ordered all-gather of each step's tokens, and the
+Covered: the max-over-ranks reduction of timings, the batch partition of the
+attention bench (16 rows) and of the end-to-end run (32 rows), the
+rank-ordered all-gather of each step's logits, and the
 reference arm under torchrun (rank 0 alone prints its line, every rank exits
 0).  No GPU is touched."""
 
@@ -33,24 +34,29 @@ def _rank_main(rank, world, port, out_dir):
         dev = torch.device("cpu")
         mx = bench.max_over_ranks([float(rank), 5.0 - rank, 2.5], dev, world)
         rows = bench.rows_per_rank(32, world)
-        nxt = torch.full((rows, 1), 100 + rank, dtype=torch.long)
-        gathered = torch.empty(world * rows, 1, dtype=torch.long)
-        g = bench.gather_tokens(nxt, gathered, world)
+        rows16 = bench.rows_per_rank(bench.B, world)
+        vocab = 7
+        logits = torch.full((rows, vocab), float(rank)) + torch.arange(vocab).float() * (rank + 1)
+        gathered = torch.empty(world * rows, vocab)
+        g = bench.gather_logits(logits, gathered, world)
+        mine = g[rank * rows:(rank + 1) * rows]
         with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
-            json.dump({"max": mx, "rows": rows, "gathered": g.flatten().tolist()}, f)
+            json.dump({"max": mx, "rows": rows, "rows16": rows16, "gathered": g[:, 0].tolist(),
+                       "mine_equal": bool(torch.equal(mine, logits))}, f)
     finally:
         dist.destroy_process_group()
 
 
-def test_two_gloo_ranks_reduce_shard_and_gather(tmp_path):
+def test_two_gloo_ranks_reduce_partition_and_gather_logits(tmp_path):
     world = 2
     mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     for rank in range(world):
         r = json.load(open(tmp_path / f"rank{rank}.json"))
         assert r["max"] == [1.0, 5.0, 2.5]          # slowest rank per timing, on every rank
-        assert r["rows"] == 16                      # 32 rows in two disjoint shards
-        assert r["gathered"] == [100] * 16 + [101] * 16  # rank order
+        assert r["rows"] == 16 and r["rows16"] == 8  # disjoint halves of each batch
+        assert r["gathered"] == [0.0] * 16 + [1.0] * 16  # rank order
+        assert r["mine_equal"]                       # each rank's own rows come back unchanged
 
 
 def test_reference_arm_under_torchrun_prints_one_line():
