@@ -121,6 +121,13 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// programmatic dependent launch: a primary grid lets its dependent grid start
+// early; the dependent waits (in hardware, not by spinning) for the primary's
+// completion and memory before it reads what the primary wrote.  In a grid
+// launched without the attribute the wait returns at once.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
+
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

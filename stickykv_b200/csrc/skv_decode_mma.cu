@@ -104,6 +104,7 @@ struct MmaParams {
   int Hq, Hv, G, ngrp;
   int s, s_eff, s_pad, NS, n_tp, rest, U, W, rope_rows;
   int upw, Ww;  // 8-token units per window (window_size / 8) and windows; W counts units
+  int merge_per;  // windows per merge thread (1 or 2)
   float scale_log2;
   int bnd[kMaxSplits + 1];
 };
@@ -164,9 +165,6 @@ __device__ __forceinline__ void mul_x2(float& d0, float& d1, float a0, float a1,
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
-// programmatic dependent launch (the merge kernel follows the decode kernel)
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
 
 // floor division by 2 for possibly negative numerators
 __device__ __forceinline__ int ceil_half(int x) { return (x + 1) >> 1; }
@@ -226,7 +224,6 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   const int u0 = p.bnd[split], u1 = p.bnd[split + 1];
   const int n_tiles = (u1 - u0 + 1) >> 1;
   const Regions R{p.NS, p.NS + p.n_tp, p.U, u1};
-  grid_launch_dependents();  // the merge kernel waits for this grid's completion itself
 
   unsigned char* ring = smem + (size_t)warp * C::kWarpRing;
   const uint32_t ring_s = smem_u32(ring);
@@ -687,6 +684,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
     if (fe < te) run_generic(fe, te);
   }
   cp_wait<0>();
+  grid_launch_dependents();  // the merge kernel waits for this grid's completion itself
 
   // ---- warp epilogue: totals per head ----
 #pragma unroll
@@ -759,57 +757,62 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   }
 }
 
-// Combine the splits of one (row, head group) for its query heads: the block
-// with blockIdx.x == 0 writes the output, every block adds the normalised
-// mass of its window chunk.  It is launched as a programmatic dependent of
-// the decode kernel: its blocks start while the decode's last blocks run,
-// load the score accumulator (which the decode does not touch), then wait for
-// the decode grid before reading its partials and masses.
+// Combine the splits of one (row, head group) for its query heads.  Every
+// block adds the normalised mass of a chunk of kMergeThreads windows (one
+// window per thread, all four heads); blocks 0..3 also write the output of
+// query head blockIdx.x, with the splits shared between kMergeThreads / D
+// threads per channel.  It is launched as a programmatic dependent of the
+// decode kernel: its blocks start while the decode's last blocks run, load
+// the score accumulator (which the decode does not touch), then wait for
+// the decode grid and issue every load of its partials, split statistics and
+// masses at once (one memory round trip).
 constexpr int kMergeThreads = 256;
-constexpr int kMergePer = 2;                               // windows per thread and head
-constexpr int kMergeWindows = kMergePer * kMergeThreads;   // windows per block
+constexpr int kMergeWindows = kMergeThreads;  // windows per block
+constexpr int kMergeOutBlocks = 4;            // blocks that also write an output head
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const __grid_constant__ MmaParams p) {
+  constexpr int kHalves = kMergeThreads / D;           // threads per output channel
+  constexpr int kSpl = kMaxSplits / kHalves;           // splits per thread
+  static_assert(kHalves >= 1 && kHalves * D == kMergeThreads, "merge threads");
   const int chunk = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;  // kh: query-head group
   const int kr = kh / p.ngrp, hbase = kr * p.G + 4 * (kh - kr * p.ngrp);
   const int nlive = min(4, p.G - (hbase - kr * p.G));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float s_f[4][kMaxSplits];   // split factor / L per head
   __shared__ int s_bnd[kMaxSplits + 1];
-  const int w0 = chunk * kMergeWindows, w_end = min(p.Ww, w0 + kMergeWindows);
+  __shared__ float s_o[kMergeThreads];
   float* acc = p.scores ? p.scores + ((int64_t)b * p.Hq + hbase) * p.scores_cap : nullptr;
-  float av[4][kMergePer];
+  const int w0 = chunk * kMergeWindows * p.merge_per + threadIdx.x;
+  float av[2][4];
 #pragma unroll
-  for (int hh = 0; hh < 4; ++hh)
+  for (int k = 0; k < 2; ++k) {
+    const int w = w0 + k * kMergeThreads;
+    const bool has = acc != nullptr && k < p.merge_per && w < p.Ww;
 #pragma unroll
-    for (int k = 0; k < kMergePer; ++k) {
-      const int w = w0 + threadIdx.x + k * kMergeThreads;
-      av[hh][k] = (acc && w < w_end && hh < nlive) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
-    }
+    for (int hh = 0; hh < 4; ++hh) av[k][hh] = (has && hh < nlive) ? acc[(int64_t)hh * p.scores_cap + w] : 0.f;
+  }
   for (int j = threadIdx.x; j <= p.n_split; j += kMergeThreads) s_bnd[j] = p.bnd[j];
   grid_dependency_wait();
   const float* part = p.part + ((int64_t)b * p.Hv + kh) * p.n_split * 4 * (D + 2);
   const float* ms = p.mass + ((int64_t)b * p.Hv * 4 + kh * 4) * p.W;
-  float mv[4][kMergePer];
+  // every load of this block, issued before any result is needed
+  float mv[2][4];
 #pragma unroll
-  for (int hh = 0; hh < 4; ++hh)
+  for (int k = 0; k < 2; ++k) {
+    const int w = w0 + k * kMergeThreads;
+    const bool has = acc != nullptr && k < p.merge_per && w < p.Ww && p.upw == 1;
 #pragma unroll
-    for (int k = 0; k < kMergePer; ++k) {
-      const int w = w0 + threadIdx.x + k * kMergeThreads;
-      mv[hh][k] = (acc && w < w_end && p.upw == 1) ? ms[(int64_t)hh * p.W + w] : 0.f;
-    }
-  // output partials of the first splits, loaded before the statistics exist
-  constexpr int kOut = 4 * D / kMergeThreads;  // (head, channel) pairs per thread
-  constexpr int kPre = 16;                     // splits prefetched per pair
-  float ov[kOut][kPre];
-  if (chunk == 0) {
+    for (int hh = 0; hh < 4; ++hh) mv[k][hh] = has ? ms[(int64_t)hh * p.W + w] : 0.f;
+  }
+  const int oh = chunk;                                          // output head of this block
+  const bool out_blk = oh < kMergeOutBlocks && oh < nlive;
+  const int c = threadIdx.x % D, half = threadIdx.x / D;
+  float ov[kSpl];
 #pragma unroll
-    for (int q = 0; q < kOut; ++q) {
-      const int e = threadIdx.x + q * kMergeThreads, hh = e / D, c = e - hh * D;
-#pragma unroll
-      for (int sp = 0; sp < kPre; ++sp) ov[q][sp] = sp < p.n_split ? part[(sp * 4 + hh) * (D + 2) + c] : 0.f;
-    }
+  for (int k = 0; k < kSpl; ++k) {
+    const int sp = half * kSpl + k;
+    ov[k] = (out_blk && sp < p.n_split) ? part[(sp * 4 + oh) * (D + 2) + c] : 0.f;
   }
   if (warp < 4) {  // warp hh: the split statistics of head hh
     const int hh = warp;
@@ -833,36 +836,41 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       if (lane + 32 * k < p.n_split) s_f[hh][lane + 32 * k] = f2[k] * invL;
   }
   __syncthreads();
-  if (chunk == 0) {
+  if (out_blk) {
+    float o = 0.f;
 #pragma unroll
-    for (int q = 0; q < kOut; ++q) {
-      const int e = threadIdx.x + q * kMergeThreads, hh = e / D, c = e - hh * D;
-      float o = 0.f;
-#pragma unroll
-      for (int sp = 0; sp < kPre; ++sp) o += s_f[hh][sp < p.n_split ? sp : 0] * ov[q][sp];
-#pragma unroll 8
-      for (int sp = kPre; sp < p.n_split; ++sp) o += s_f[hh][sp] * part[(sp * 4 + hh) * (D + 2) + c];
-      if (hh < nlive) st_f32((T*)p.out + b * p.o_sb + (hbase + hh) * p.o_sh + c, o);
+    for (int k = 0; k < kSpl; ++k) {
+      const int sp = half * kSpl + k;
+      o += s_f[oh][sp < p.n_split ? sp : 0] * ov[k];
     }
+    if (kHalves > 1) {
+      s_o[threadIdx.x] = o;
+      __syncthreads();
+      if (half == 0) {
+#pragma unroll
+        for (int h = 1; h < kHalves; ++h) o += s_o[threadIdx.x + h * D];
+      }
+    }
+    if (half == 0) st_f32((T*)p.out + b * p.o_sb + (hbase + oh) * p.o_sh + c, o);
   }
   if (acc == nullptr) return;
+  auto split_of = [&](int u) {  // last split with bnd <= u
+    int lo = 0, hi = p.n_split - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_bnd[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
 #pragma unroll
-  for (int k = 0; k < kMergePer; ++k) {
-    const int w = w0 + threadIdx.x + k * kMergeThreads;
-    if (w >= w_end) continue;
-    auto split_of = [&](int u) {  // last split with bnd <= u
-      int lo = 0, hi = p.n_split - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_bnd[mid] <= u) lo = mid; else hi = mid - 1;
-      }
-      return lo;
-    };
+  for (int k = 0; k < 2; ++k) {
+    const int w = w0 + k * kMergeThreads;
+    if (k >= p.merge_per || w >= p.Ww) break;
     if (p.upw == 1) {
       const int lo = split_of(p.NS + w);
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh)
-        if (hh < nlive) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + mv[hh][k] * s_f[hh][lo];
+        if (hh < nlive) acc[(int64_t)hh * p.scores_cap + w] = av[k][hh] + mv[k][hh] * s_f[hh][lo];
     } else {  // a window of several units, each normalised by its own split
       float sum[4] = {0.f, 0.f, 0.f, 0.f};
       for (int j = 0; j < p.upw && w * p.upw + j < p.W; ++j) {
@@ -872,7 +880,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_mma_merge_kernel(const _
       }
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh)
-        if (hh < nlive) acc[(int64_t)hh * p.scores_cap + w] = av[hh][k] + sum[hh];
+        if (hh < nlive) acc[(int64_t)hh * p.scores_cap + w] = av[k][hh] + sum[hh];
     }
   }
 }
@@ -887,7 +895,8 @@ int max_splits(int U) {
 template <int D>
 void plan_splits(MmaParams& p) {
   // Ranges hold equal estimated cost (the per-tile costs of the kernel's
-  // tile classes); the split count fills whole waves of resident CTAs.
+  // tile classes); the split count fills one or two whole waves of resident
+  // CTAs.
   const int TB = p.NS + p.n_tp, UF = TB + p.rest / 8;
   auto clampi = [](int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); };
   // cost of units [0, u), in half-tile units (2x the per-tile cost per pair)
@@ -897,7 +906,10 @@ void plan_splits(MmaParams& p) {
   };
   const int units = p.B * p.Hv;
   const int slots = 148 * (D == 64 ? 4 : 2);
-  int n = max(1, (2 * slots) / max(1, units));
+  // one wave of resident CTAs when its ranges fit kMaxUnitsPerSplit (small
+  // batches: every CTA's fixed cost paid once), else two waves
+  int n = max(1, slots / max(1, units));
+  if (ceil_div(p.U, n) > kMaxUnitsPerSplit) n = max(1, (2 * slots) / max(1, units));
   n = max(n, ceil_div(p.U, kMaxUnitsPerSplit));
   n = min(n, kMaxSplits);
   n = min(n, max(1, p.U / 16));
@@ -935,7 +947,9 @@ int launch_mma(MmaParams& p, cudaStream_t stream) {
   decode_mma_kernel<T, D><<<dim3(p.n_split, p.Hv, p.B), kThreads, C::kSmemBytes, stream>>>(p);
   SKV_CHECK_LAUNCH();
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(p.scores ? max(1, ceil_div(p.Ww, kMergeWindows)) : 1, p.Hv, p.B);
+  // two windows per thread when many (row, head group)s fill the GPU anyway
+  p.merge_per = p.B * p.Hv >= 64 ? 2 : 1;
+  cfg.gridDim = dim3(max(kMergeOutBlocks, p.scores ? ceil_div(p.Ww, kMergeWindows * p.merge_per) : 0), p.Hv, p.B);
   cfg.blockDim = dim3(kMergeThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;

@@ -74,6 +74,7 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int b = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
+  grid_launch_dependents();  // the apply kernel's blocks that read the selection wait for it
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                   // [E]
   int* hist = reinterpret_cast<int*>(keys + (p.E > 0 ? p.E : 1));           // [256]
   int* scan = hist + 256;                                                   // [32]
@@ -569,10 +570,27 @@ __device__ void move_v_block(const EvictParams& p, const ApplyGrid& a, int bid) 
   }
 }
 
+// Launched as a programmatic dependent of the select kernel.  With the int4
+// tier the fp tokens that stay fp are the sinks and the local windows, whose
+// new positions follow from the plan's counts alone, so the move blocks (the
+// bulk of the bytes) run alongside the selection; blocks that read the
+// selection (demotion, gather, and every move in reference mode) wait for it.
+// The waiting blocks come last in the grid.
 template <typename T, int D>
 __global__ void __launch_bounds__(kApplyThreads, 3) evict_apply_kernel(EvictParams p, ApplyGrid a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int bid = blockIdx.x;
+  if (bid < a.n_move_v + a.n_move) {
+    if (!p.tier) grid_dependency_wait();
+    if (bid < a.n_move_v) {  // the short value copies first, then the key re-rotation
+      move_v_block<T, D>(p, a, bid);
+      return;
+    }
+    move_k_block<T, D>(p, a, bid - a.n_move_v);
+    return;
+  }
+  bid -= a.n_move_v + a.n_move;
+  grid_dependency_wait();
   if constexpr (D % kQGroup == 0) {  // the int4 tier needs whole 32-channel groups
     if (bid < a.n_demote) {
       demote_block<T, D>(p, a, bid, smem_raw);
@@ -580,16 +598,7 @@ __global__ void __launch_bounds__(kApplyThreads, 3) evict_apply_kernel(EvictPara
     }
   }
   bid -= a.n_demote;
-  if (bid < a.n_gather) {
-    gather_block(p, a, bid);
-    return;
-  }
-  bid -= a.n_gather;
-  if (bid < a.n_move_v) {  // the short value copies first, then the key re-rotation
-    move_v_block<T, D>(p, a, bid);
-    return;
-  }
-  move_k_block<T, D>(p, a, bid - a.n_move_v);
+  if (bid < a.n_gather) gather_block(p, a, bid);
 }
 
 template <typename T, int D>
@@ -632,8 +641,21 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
   if (blocks == 0) return SKV_OK;
   if (blocks > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
   const size_t smem = a.n_demote ? quant_scratch_bytes(D) : 0;
-  evict_apply_kernel<T, D><<<(unsigned)blocks, kApplyThreads, smem, stream>>>(p, a);
-  SKV_CHECK_LAUNCH();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(kApplyThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, evict_apply_kernel<T, D>, p, a);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return SKV_ERR_CUDA;
+  }
   return SKV_OK;
 }
 
