@@ -575,30 +575,30 @@ __device__ void move_v_block(const EvictParams& p, const ApplyGrid& a, int bid) 
 // new positions follow from the plan's counts alone, so the move blocks (the
 // bulk of the bytes) run alongside the selection; blocks that read the
 // selection (demotion, gather, and every move in reference mode) wait for it.
-// The waiting blocks come last in the grid.
+// The waiting blocks come first in the grid: they hold a few slots while the
+// moves stream and then run beside the rest of them, not as a tail.
 template <typename T, int D>
 __global__ void __launch_bounds__(kApplyThreads, 3) evict_apply_kernel(EvictParams p, ApplyGrid a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int bid = blockIdx.x;
-  if (bid < a.n_move_v + a.n_move) {
-    if (!p.tier) grid_dependency_wait();
-    if (bid < a.n_move_v) {  // the short value copies first, then the key re-rotation
-      move_v_block<T, D>(p, a, bid);
-      return;
+  if (bid < a.n_demote + a.n_gather) {
+    grid_dependency_wait();
+    if constexpr (D % kQGroup == 0) {  // the int4 tier needs whole 32-channel groups
+      if (bid < a.n_demote) {
+        demote_block<T, D>(p, a, bid, smem_raw);
+        return;
+      }
     }
-    move_k_block<T, D>(p, a, bid - a.n_move_v);
+    gather_block(p, a, bid - a.n_demote);
     return;
   }
-  bid -= a.n_move_v + a.n_move;
-  grid_dependency_wait();
-  if constexpr (D % kQGroup == 0) {  // the int4 tier needs whole 32-channel groups
-    if (bid < a.n_demote) {
-      demote_block<T, D>(p, a, bid, smem_raw);
-      return;
-    }
+  bid -= a.n_demote + a.n_gather;
+  if (!p.tier) grid_dependency_wait();
+  if (bid < a.n_move_v) {  // the short value copies first, then the key re-rotation
+    move_v_block<T, D>(p, a, bid);
+    return;
   }
-  bid -= a.n_demote;
-  if (bid < a.n_gather) gather_block(p, a, bid);
+  move_k_block<T, D>(p, a, bid - a.n_move_v);
 }
 
 template <typename T, int D>
