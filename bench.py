@@ -369,9 +369,12 @@ def run_ours(args, rank, world, dev):
     e2e_ms = e0.elapsed_time(e1)
     h2d = din.numel() * 2
     d2h = hout[0].numel() * 2
-    evict_avg = float(np.mean(evict_ms)) if evict_ms else 0.0
-    ms, e2e_ms, attn_ms, evict_avg, host_us = max_over_ranks([ms, e2e_ms, attn_ms, evict_avg, host_us], dev,
-                                                             world)
+    evict_host = float(np.mean(evict_ms)) if evict_ms else 0.0
+    ms, e2e_ms, attn_ms, evict_host, host_us = max_over_ranks([ms, e2e_ms, attn_ms, evict_host, host_us], dev,
+                                                              world)
+    # GPU time of one eviction, from the graph-timed numbers: the steps of a
+    # cycle beyond their decode launches, per eviction (WS steps apart)
+    evict_avg = max(0.0, (ms / args.steps - attn_ms) * WS)
     del cache
     torch.cuda.empty_cache()
     model = None
@@ -422,7 +425,10 @@ def run_ours(args, rank, world, dev):
         "evict": {"algorithmic_bytes": evict_bytes, "avg_us": evict_avg * 1e3,
                   "achieved_gbs": evict_bytes / (evict_avg * 1e-3) / 1e9 if evict_avg else None,
                   "frac": evict_bytes / (evict_avg * 1e-3) / 1e9 / peak if evict_avg else None,
-                  "note": "append + select + apply of an evicting update(), events on the stream"},
+                  "host_driven_us": evict_host * 1e3,
+                  "note": "GPU time per eviction = (ms_per_step - decode launch) x window_size from the graph-timed "
+                          "steps (append + select + apply, select overlapped by the apply's moves); "
+                          "host_driven_us: events around an evicting update() called from Python"},
         "host_us_per_step": host_us,
         "e2e": {"value": B * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -486,8 +492,10 @@ def run_e2e(args, rank, world, dev):
     """End-to-end decode through transformers: a Llama-3.2-1B-shaped decoder
     (random N(0,0.02) weights, bf16) prefills 8192 random tokens per row and
     greedily decodes 256 tokens with the windowed cache (budget 0.40, int4
-    tier).  The global batch of 32 rows is split across the ranks; decode
-    tokens/s = rows x steps / decode time (max over ranks), prefill excluded.
+    tier).  The global batch of 32 rows is split across the ranks.  Decoding
+    runs eagerly until the cache reaches its steady state, then the remaining
+    steps replay CUDA graphs of the whole forward (DecodeGraphs); decode
+    tokens/s = rows x steps / time over those steps (max over ranks).
     At N > 1 the ranks all-gather each step's logits.  Also reported,
     as the reference's perf runner does: time to first token (the prefill
     forward), time per output token and peak device memory; `--e2e-budget`
@@ -497,7 +505,7 @@ def run_e2e(args, rank, world, dev):
     import torch.distributed as dist
     from transformers import LlamaConfig, LlamaForCausalLM
 
-    from stickykv_b200 import WindowedCache, WindowedCacheConfig, install_score_hooks
+    from stickykv_b200 import DecodeGraphs, WindowedCache, WindowedCacheConfig, install_score_hooks
 
     c = dict(E2E)
     if args.e2e_prompt:
@@ -534,28 +542,59 @@ def run_e2e(args, rank, world, dev):
         time.sleep(0.3)
         if world > 1:
             dist.barrier()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         # every step the ranks all-gather the batch's last-position logits
         # (NCCL over NVLink), the only collective of the run; each rank keeps
         # decoding its own rows from its slice of the gathered logits
         gathered = (torch.empty(world * rows, c["vocab"], dtype=torch.bfloat16, device=dev)
                     if world > 1 else None)
-        t0.record(stream)
-        for _ in range(c["decode"] - 1):
-            out = model(input_ids=nxt, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        tok = nxt.clone()
+
+        def decode_step(j=0):
+            out = model(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
             logits = gather_logits(out.logits[:, -1].contiguous(), gathered, world)
-            nxt = logits[rank * rows:(rank + 1) * rows].argmax(-1, keepdim=True)
+            tok.copy_(logits[rank * rows:(rank + 1) * rows].argmax(-1, keepdim=True))
+
+        total = c["decode"] - 1
+        # eager steps until the cache is in steady state (two evictions behind
+        # it, at a period boundary), timed on their own
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        n_eager = 0
+        while n_eager < total and not DecodeGraphs.ready(cache):
+            decode_step()
+            n_eager += 1
+        e1.record(stream)
+        graphs = None
+        if total - n_eager >= 2 * DecodeGraphs.period_of(cache) and not args.e2e_eager:
+            graphs = DecodeGraphs(cache, decode_step, stream=stream)
+        torch.cuda.synchronize(dev)
+        sampler = ClockSampler(dev.index if dev.index is not None else 0)
+        sampler.start()
+        time.sleep(0.3)
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_timed = total - n_eager
+        t0.record(stream)
+        if graphs is not None:
+            graphs.replay(n_timed)
+        else:
+            for _ in range(n_timed):
+                decode_step()
         t1.record(stream)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         clocks = sampler.stop()
+        used_graphs = graphs is not None
+        del graphs
     handles.remove()
-    dec_ms, pre_ms, peak = max_over_ranks(
-        [t0.elapsed_time(t1), p0.elapsed_time(p1), torch.cuda.max_memory_allocated(dev)], dev, world)
+    dec_ms, pre_ms, eager_ms, peak = max_over_ranks(
+        [t0.elapsed_time(t1), p0.elapsed_time(p1), e0.elapsed_time(e1), torch.cuda.max_memory_allocated(dev)],
+        dev, world)
     if rank != 0:
         return None
-    steps = c["decode"] - 1
+    steps = n_timed
     total_rows = rows * world
     return {
         "metric": "e2e decode tokens/s (Llama-3.2-1B shape, 8k prompt, int4 tier)", "unit": "tokens/s",
@@ -569,6 +608,10 @@ def run_e2e(args, rank, world, dev):
                    "cache_budget": budget, "retained_tokens": cache.get_seq_length(0),
                    "parallelism": f"{world} batch shards"},
         "prefill_ms": pre_ms, "ttft_ms": pre_ms, "tpot_ms": dec_ms / steps,
+        "eager_steps": n_eager, "eager_tpot_ms": eager_ms / max(1, n_eager),
+        "launch": ("timed steps replay CUDA graphs of the whole forward (steady state, after the "
+                   f"{n_eager} eager steps that reach it)") if used_graphs else "eager",
+        "nccl_ranks": world if world > 1 else None,
         "peak_mem_gib": peak / 2 ** 30, "clocks": clocks,
     }
 
@@ -732,6 +775,8 @@ def main():
     ap.add_argument("--e2e-prompt", type=int, default=0)
     ap.add_argument("--e2e-decode", type=int, default=0)
     ap.add_argument("--e2e-budget", type=float, default=0.0)
+    ap.add_argument("--e2e-eager", action="store_true",
+                    help="decode the model run eagerly (no CUDA-graph replay of its steps)")
     ap.add_argument("--no-model", action="store_true",
                     help="leave the Llama-3.2-1B-shaped model run out of the default line")
     ap.add_argument("--no-tier", action="store_true",

@@ -235,6 +235,18 @@ int skv_prefill_attention(const skv_layer_desc* layer, int32_t T, const void* q,
                           void* stream);
 
 /*
+ * The retained cache as plain keys and values in logical order,
+ * k_out/v_out [batch][num_kv_heads][seq_len][head_dim] (kv_dtype, contiguous):
+ * the reference's CacheState.key_states / value_states
+ * (modules/windowed_cache/state.py:20-35), which its flash score hook
+ * (modules/windowed_cache/hooks.py:218) and parity runner read.  fp tokens
+ * are copied; int4 tier tokens are dequantised (code * scale + zero in fp32)
+ * and their keys rotated from the page frame to their current position.
+ */
+int skv_materialize(const skv_layer_desc* layer, int32_t seq_len, int32_t tier_pages, void* k_out,
+                    void* v_out, void* stream);
+
+/*
  * Quantise n_pages*8 kv_dtype tokens (k/v [n_pages*8][head_dim], keys
  * post-RoPE at positions first_pos..) into int4 pages (keys in their
  * page-relative frame), out [n_pages][page_bytes].

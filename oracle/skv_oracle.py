@@ -726,6 +726,32 @@ class OracleCache:
         kc, ks, kz, vc, vs, vz = self.tier_codes
         return dequant_group32(kc, ks, kz), dequant_group32(vc, vs, vz)
 
+    def materialize(self):
+        """Every retained token as plain keys and values [B,H,T,D] in logical
+        order (the reference's ``CacheState.key_states``/``value_states``,
+        state.py:20-35): fp tokens as stored; tier tokens dequantised
+        (``code*scale + zero`` in fp32) with their keys rotated from the page
+        frame to their current position, ``R(P)`` of the stored vector for a
+        page starting at P (fp32, no fused multiply-add), then rounded to the
+        KV dtype."""
+        if self.n_tier_tokens == 0:
+            return self.k.copy(), self.v.copy()
+        s = self.r.num_sink_tokens
+        n_s = min(s, self.k.shape[2])
+        tk, tv = self.tier_dequant()
+        D = tk.shape[-1]
+        h = D // 2
+        pos = s + PAGE_TOKENS * (np.arange(self.n_tier_tokens) // PAGE_TOKENS)
+        c = self.cos[pos][:, :h].astype(np.float32)
+        sn = self.sin[pos][:, :h].astype(np.float32)
+        x, y = tk[..., :h], tk[..., h:]
+        kx = ((x * c).astype(np.float32) - (y * sn).astype(np.float32)).astype(np.float32)
+        ky = ((y * c).astype(np.float32) + (x * sn).astype(np.float32)).astype(np.float32)
+        keys = round_to(np.concatenate([kx, ky], axis=-1), self.dtype)
+        vals = round_to(tv, self.dtype)
+        return (np.concatenate([self.k[:, :, :n_s], keys, self.k[:, :, n_s:]], axis=2),
+                np.concatenate([self.v[:, :, :n_s], vals, self.v[:, :, n_s:]], axis=2))
+
     def decode_attention(self, q: np.ndarray, scaling: float):
         """Attention of a decode query over the current cache -> (out, mass)."""
         s = self.r.num_sink_tokens

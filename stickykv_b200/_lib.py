@@ -27,7 +27,7 @@ EXPORTS = (
     "skv_evict_plan_compute", "skv_append", "skv_decode_workspace_size", "skv_decode_attention",
     "skv_evict_workspace_size", "skv_evict", "skv_prefill_workspace_size",
     "skv_prefill_attention", "skv_pack_pages", "skv_decode_attention_noalloc",
-    "skv_decode_attention_append",
+    "skv_decode_attention_append", "skv_materialize",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -90,6 +90,7 @@ def _declare(lib: C.CDLL) -> None:
         "skv_prefill_attention": (C.c_int, [C.POINTER(LayerDesc), I32, P, P, P, P, F, P, I32, P,
                                             SZ, P]),
         "skv_pack_pages": (C.c_int, [C.POINTER(LayerDesc), P, P, I32, I32, P, P]),
+        "skv_materialize": (C.c_int, [C.POINTER(LayerDesc), I32, I32, P, P, P]),
         "skv_decode_attention_noalloc": (C.c_int, [C.POINTER(LayerDesc), I32, I32, P, I64, I64, P,
                                                    I64, I64, F, P, I32, P]),
         "skv_decode_attention_append": (C.c_int, [C.POINTER(LayerDesc), I32, I32, P, P, I64, I64, P,

@@ -90,9 +90,11 @@ class LayerState:
         self.next_window_id = 0
         self.last_update_prefill = False
         self.allocated = False
+        self.evictions = 0  # evictions run so far (steady state after the second)
         # one decode token whose append is fused into the next decode call
         self.pending: Optional[Tuple[Tensor, Tensor]] = None
         self.flush = None  # writes a pending token (set by the cache)
+        self.materialize = None  # (keys, values) of an int4-tier cache (set by the cache)
         self.decode_ws, self.decode_ws_T = 0, 0  # decode workspace bytes, valid up to decode_ws_T
         # geometry copied at allocation
         self.B = self.Hkv = self.Hq = self.D = 0
@@ -109,9 +111,7 @@ class LayerState:
         if self.pending is not None:
             self.flush(self)
         if self.tier_pages:
-            raise NotImplementedError(
-                "key_states/value_states of an int4-tier cache are not materialised; "
-                "read the fp store and the int4 pages instead")
+            return self.materialize(self)[0 if which == "k" else 1]
         side = self.sides[self.cur]
         buf = side.k if which == "k" else side.v
         s = min(self.num_sink, self.T)
@@ -121,7 +121,8 @@ class LayerState:
 
     @property
     def key_states(self) -> Optional[Tensor]:
-        """[B, Hkv, T, D] post-RoPE keys in logical order (a copy)."""
+        """[B, Hkv, T, D] post-RoPE keys in logical order (a copy; int4 tier
+        tokens dequantised and rotated to their current positions)."""
         return self._fp_view("k")
 
     @property
@@ -250,7 +251,19 @@ class WindowedCache(_HFCacheBase):
     def _new_state(self) -> LayerState:
         st = LayerState()
         st.flush = self._flush
+        st.materialize = self._materialize
         return st
+
+    def _materialize(self, st: LayerState) -> Tuple[Tensor, Tensor]:
+        """Keys and values of every retained token, tier included, as plain
+        [B, Hkv, T, D] tensors in the KV dtype (skv_materialize)."""
+        k = torch.empty(st.B, st.Hkv, st.T, st.D, dtype=st.dtype, device=st.device)
+        v = torch.empty_like(k)
+        d = self._desc(st, st.sides[st.cur])
+        with _on(st.device):
+            check(lib().skv_materialize(C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(),
+                                        _stream(st.device)), "skv_materialize")
+        return k, v
 
     # -- allocation ------------------------------------------------------------------------
     def _caps(self, P: int) -> Tuple[int, int, int, int]:
@@ -509,6 +522,7 @@ class WindowedCache(_HFCacheBase):
         st.T = plan.seq_len_new
         st.tier_pages = plan.tier_pages_new
         st.W = plan.retained_windows
+        st.evictions += 1
 
     def _token_indices(self, retained: Tensor, total: int) -> Tensor:
         """Retained windows -> token indices (reference policy.py:152-209); telemetry only."""

@@ -29,6 +29,8 @@ int decode_mma(const skv_layer_desc* L, int T, int tier_pages, const void* q, in
 int evict_dispatch(EvictParams& p, cudaStream_t stream);
 int pack_pages_dispatch(const skv_layer_desc* L, const void* k, const void* v, int first_pos,
                         int n_pages, uint8_t* out, cudaStream_t stream);
+int materialize_dispatch(const skv_layer_desc* L, int T_len, int tier_pages, void* k_out, void* v_out,
+                         cudaStream_t stream);
 size_t prefill_ws_size(const skv_layer_desc* L, int T);
 int prefill_dispatch(const skv_layer_desc* L, int T, const void* q, const void* k, const void* v,
                      void* out, float scaling, float* scores, int scores_cap, void* ws,
@@ -309,6 +311,16 @@ int skv_prefill_attention(const skv_layer_desc* L, int32_t T, const void* q, con
   if (scores && scores_cap < g.num_windows()) return SKV_ERR_CAPACITY;
   if (!ws || ws_bytes < skv_prefill_workspace_size(L, T)) return SKV_ERR_WORKSPACE;
   return prefill_dispatch(L, T, q, k, v, out, scaling, scores, scores_cap, ws, (cudaStream_t)stream);
+}
+
+int skv_materialize(const skv_layer_desc* L, int32_t seq_len, int32_t tier_pages, void* k_out, void* v_out,
+                    void* stream) {
+  int rc = check_layer(L);
+  if (rc) return rc;
+  if (seq_len <= 0 || !k_out || !v_out) return SKV_ERR_INVALID_ARG;
+  if ((rc = check_counts(L, seq_len, tier_pages))) return rc;
+  if (tier_pages > 0 && L->rope_positions < L->num_sink + tier_pages * kPageTokens) return SKV_ERR_CAPACITY;
+  return materialize_dispatch(L, seq_len, tier_pages, k_out, v_out, (cudaStream_t)stream);
 }
 
 int skv_pack_pages(const skv_layer_desc* L, const void* k, const void* v, int32_t first_pos,

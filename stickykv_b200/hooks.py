@@ -106,14 +106,26 @@ def stickykv_attention(module: nn.Module, query: torch.Tensor, key: torch.Tensor
     return cache.decode_attention(layer, query, scaling), None
 
 
+def padding_mask(*args, attention_mask: Optional[torch.Tensor] = None, **kwargs) -> Optional[torch.Tensor]:
+    """Mask function of the ``stickykv_b200`` implementation: no mask at all
+    for a batch without a 2-D padding mask (the causal pattern is the
+    kernels' own, also under CUDA-graph capture, where transformers' sdpa
+    function would materialise one), else the sdpa function's answer, which
+    is None for an unpadded batch and a 4-D mask for a padded one (that the
+    attention then refuses)."""
+    if attention_mask is None:
+        return None
+    from transformers.masking_utils import sdpa_mask
+    return sdpa_mask(*args, attention_mask=attention_mask, **kwargs)
+
+
 def _register_attention() -> None:
     from transformers import AttentionInterface
-    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+    from transformers.masking_utils import AttentionMaskInterface
     AttentionInterface.register(ATTN_IMPLEMENTATION, stickykv_attention)
     # transformers builds no mask for an implementation without a mask
-    # function; the sdpa one skips the mask (None) for unpadded causal batches
-    # and materialises it when a row is padded, which the attention refuses
-    AttentionMaskInterface.register(ATTN_IMPLEMENTATION, sdpa_mask)
+    # function, so a padded batch would pass unnoticed
+    AttentionMaskInterface.register(ATTN_IMPLEMENTATION, padding_mask)
 
 
 def install_score_hooks(model: nn.Module, cache: Any, config: Any) -> HookHandles:

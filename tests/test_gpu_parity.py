@@ -533,3 +533,22 @@ def test_fused_append_decode_matches_append_then_decode(dt, D, G, tier):
     for name, a, b in zip(("out", "scores", "k", "v"), *runs):
         bad = (a != b) & ~(torch.isnan(a) & torch.isnan(b))
         assert not bad.any(), f"{name}: {int(bad.sum())} differ, first at {bad.nonzero()[0].tolist()} (T0={T0})"
+
+
+@pytest.mark.parametrize("dt,D", [("f16", 64), ("bf16", 128), ("f32", 64)])
+def test_int4_tier_key_and_value_states_materialised(dt, D):
+    """key_states / value_states of an int4-tier cache (skv_materialize): fp
+    tokens as stored, tier tokens dequantised and rotated to their current
+    positions, bit-exact against the oracle after each eviction."""
+    n = 0
+    for kind, *rest in _drive_pair(dt, tier=True, D=D, P=403, steps=18, seed=9):
+        if kind != "evict":
+            continue
+        cache, oc = rest
+        st = cache._states[0]
+        assert st.tier_pages > 0
+        k, v = oc.materialize()
+        np.testing.assert_array_equal(to_np(st.key_states), k)
+        np.testing.assert_array_equal(to_np(st.value_states), v)
+        n += 1
+    assert n == 2

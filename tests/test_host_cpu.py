@@ -199,13 +199,16 @@ def test_hook_handles_idempotent_and_null_telemetry():
 
 def test_padded_batches_are_refused():
     """transformers builds no mask for an unknown attention implementation;
-    this package registers the sdpa mask function with its own, which skips
-    the mask for unpadded causal batches, so a mask reaching the attention
-    means padding, and the attention refuses it."""
+    this package registers a mask function with its own that builds no mask
+    without a 2-D padding mask and otherwise defers to the sdpa one (None for
+    an unpadded batch), so a mask reaching the attention means padding, and
+    the attention refuses it."""
     from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS
     from stickykv_b200.hooks import ATTN_IMPLEMENTATION, _register_attention, stickykv_attention
     _register_attention()
     assert ATTN_IMPLEMENTATION in ALL_MASK_ATTENTION_FUNCTIONS
+    from stickykv_b200.hooks import padding_mask
+    assert padding_mask(1, 1, 5, attention_mask=None) is None  # no padding mask: no mask, even when capturing
 
     class Attn(torch.nn.Module):
         layer_idx = 0

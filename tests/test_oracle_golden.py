@@ -314,3 +314,29 @@ def test_tie_fixture_puts_equal_means_across_the_threshold():
         assert tied.size > k - n_above  # more tied windows than places left
         kept_tied = [w for w in ret[b, :k] if ev[w] == kth]
         np.testing.assert_array_equal(kept_tied, tied[: k - n_above])
+
+
+def test_materialized_tier_attends_like_the_page_frame():
+    """Attention over the materialised keys and values (tier rotated to its
+    current positions) equals the tiered attention that rotates the query to
+    each page instead (fp32 cache, so no rounding between the two)."""
+    rng = np.random.default_rng(8)
+    B, Hkv, G, D, P = 2, 2, 4, 64, 203
+    inv = (1.0 / (500000.0 ** (np.arange(0, D, 2) / D))).astype(np.float32)
+    cos, sin = O.rope_tables(inv, P + 64)
+    oc = O.OracleCache(O.resolve(8, 4, 0.25, 0.4, P, Hkv, D, 4, 16), "f32", cos, sin, tier=True)
+    oc.update(rng.standard_normal((B, Hkv, P, D)).astype(np.float32),
+              rng.standard_normal((B, Hkv, P, D)).astype(np.float32), None)
+    oc.add_scores(rng.random((B, Hkv * G, -(-(P - 4) // 8))).astype(np.float32))
+    for _ in range(9):
+        kv = rng.standard_normal((B, Hkv, 1, D)).astype(np.float32)
+        oc.update(kv, kv, None)
+    assert oc.n_tier_tokens > 0
+    k, v = oc.materialize()
+    assert k.shape[2] == oc.seq_length
+    q = rng.standard_normal((B, Hkv * G, D)).astype(np.float32)
+    out_frame, mass_frame = oc.decode_attention(q, D ** -0.5)
+    out_plain, mass_plain = O.tiered_decode_attention(q, k[:, :, :4], v[:, :, :4], None, None, k[:, :, 4:],
+                                                      v[:, :, 4:], 4, 8, D ** -0.5)
+    np.testing.assert_allclose(out_plain, out_frame, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(mass_plain, mass_frame, rtol=1e-4, atol=1e-6)
