@@ -250,7 +250,7 @@ def run_ours(args, rank, world, dev):
     import torch
     import torch.distributed as dist
 
-    rows = rows_per_rank(B, world)
+    rows = args.rows or rows_per_rank(B, world)
     cache = build_steady_cache(dev, seed=1 + rank, rows=rows, tier=not args.no_tier)
     st = cache._states[0]
     g = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -397,13 +397,13 @@ def run_ours(args, rank, world, dev):
         except (OSError, ValueError):
             traffic = None
     line = {
-        "metric": METRIC, "value": B * args.steps / (ms * 1e-3), "unit": UNIT,
+        "metric": METRIC, "value": rows * world * args.steps / (ms * 1e-3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "f16 (int4 tier codes, fp32 accumulate)", "data": "synthetic N(0,1), seeded",
         "config": {"workload": "decode-attention + eviction step of one layer, 32k context, "
                                + ("all-fp16 retained cache" if args.no_tier else "int4 tier"),
-                   "global_batch": B, "rows_per_gpu": rows, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "global_batch": rows * world, "rows_per_gpu": rows, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
                    "context": CTX, "cache_budget": BUDGET, "window_size": WS, "sinks": SINKS, "local": LOCAL,
                    "retained_tokens": st.T, "int4_tokens": st.tier_pages * 8,
                    "evictions_in_timed_region": n_evict,
@@ -430,7 +430,7 @@ def run_ours(args, rank, world, dev):
                           "steps (append + select + apply, select overlapped by the apply's moves); "
                           "host_driven_us: events around an evicting update() called from Python"},
         "host_us_per_step": host_us,
-        "e2e": {"value": B * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
+        "e2e": {"value": rows * world * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": gpu_launches,
         "clocks": clocks,
@@ -777,6 +777,8 @@ def main():
     ap.add_argument("--e2e-budget", type=float, default=0.0)
     ap.add_argument("--e2e-eager", action="store_true",
                     help="decode the model run eagerly (no CUDA-graph replay of its steps)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows per GPU of the attention workload (default: the 16 rows partitioned over the GPUs)")
     ap.add_argument("--no-model", action="store_true",
                     help="leave the Llama-3.2-1B-shaped model run out of the default line")
     ap.add_argument("--no-tier", action="store_true",

@@ -42,6 +42,8 @@ class DecodeGraphs:
         if not self.ready(cache):
             raise RuntimeError("DecodeGraphs needs a cache in steady state at a period boundary "
                                "(see DecodeGraphs.ready)")
+        if stream is not None and stream.cuda_stream == 0:
+            stream = None  # capture needs a side stream; torch picks one for None
         self.period = self.period_of(cache)
         self.pos = 0
         self.graphs: List[torch.cuda.CUDAGraph] = []
