@@ -239,6 +239,153 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   }
 }
 
+// Select for an eviction that drops only a few evictable windows (in steady
+// state exactly one: one window leaves the local region between two
+// evictions).  The kept set of the radix path -- the k largest head means,
+// the lowest window index first among equal keys -- is the complement of the
+// m = E - k smallest keys taken in (key ascending, index descending) order,
+// so m block-wide argmin passes find the dropped windows, every kept window's
+// chronological slot is its index minus the dropped windows before it, and
+// with the int4 tier the few entrants take the lowest free pages found by
+// warp ballots.  Used when m <= kDropMax and (with the tier) at most 32
+// candidate windows can enter the tier.
+constexpr int kDropMax = 8;
+
+__device__ __forceinline__ uint64_t drop_order(uint32_t key, int w) {
+  return ((uint64_t)key << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)w);  // min: key asc, index desc
+}
+
+__global__ void __launch_bounds__(kSelectThreads) evict_select_drop_kernel(EvictParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  grid_launch_dependents();  // the apply kernel's blocks that read the selection wait for it
+  const int E = p.E, k = p.kprime, m = E - k;
+  const int n_tw_old = p.n_tier_old_tok / p.ws, n_cand = E - n_tw_old;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                   // [E]
+  int* tbl = reinterpret_cast<int*>(keys + E);                              // [n_tw_old * ppw]
+  unsigned char* used = reinterpret_cast<unsigned char*>(tbl + (p.tier ? n_tw_old * p.ppw + 1 : 1));
+  __shared__ uint64_t s_best[32];
+  __shared__ int s_drop[kDropMax];
+  __shared__ int s_ent[32];
+  __shared__ int s_free[32 * 4];
+
+  // 1. head-mean keys (heads summed in order, as the radix path), the row's
+  //    logical tier page table, cleared page-use flags
+  const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
+  for (int w = tid; w < E; w += nt) {
+    float acc = 0.f;
+    int h = 0;
+    for (; h + 32 <= p.Hq; h += 32) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc = __fadd_rn(acc, v[i]);
+    }
+    for (; h + 16 <= p.Hq; h += 16) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc = __fadd_rn(acc, v[i]);
+    }
+    for (; h < p.Hq; ++h) acc = __fadd_rn(acc, rowp[(int64_t)h * p.scores_cap + w]);
+    keys[w] = orderable(__fdiv_rn(acc, (float)p.Hq));
+  }
+  if (p.tier) {
+    for (int i = tid; i < p.page_cap; i += nt) used[i] = 0;
+    for (int i = tid; i < n_tw_old * p.ppw; i += nt) tbl[i] = p.table_src[(int64_t)b * p.page_cap + i];
+    for (int c = tid; c < n_cand; c += nt) p.entrant[(int64_t)b * p.W + c] = -1;
+  }
+  __syncthreads();
+  // 2. the m dropped windows, one block-wide argmin each
+  for (int it = 0; it < m; ++it) {
+    uint64_t best = ~0ull;
+    for (int w = tid; w < E; w += nt) {
+      bool gone = false;
+      for (int d = 0; d < it; ++d) gone |= s_drop[d] == w;
+      if (!gone) best = min(best, drop_order(keys[w], w));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (lane == 0) s_best[warp] = best;
+    __syncthreads();
+    if (warp == 0) {
+      uint64_t v = lane < (nt >> 5) ? s_best[lane] : ~0ull;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (lane == 0) s_drop[it] = (int)(0xFFFFFFFFu - (uint32_t)v);
+    }
+    __syncthreads();
+  }
+  // 3. chronological slots: a kept window's slot is its index minus the
+  //    dropped windows before it; kept tier windows keep their pages,
+  //    candidates that stay become entrants
+  for (int w = tid; w < E; w += nt) {
+    int before = 0;
+    bool gone = false;
+    for (int d = 0; d < m; ++d) {
+      before += s_drop[d] < w;
+      gone |= s_drop[d] == w;
+    }
+    if (gone) continue;
+    const int j = w - before;
+    p.retained[(int64_t)b * p.R + j] = w;
+    if (p.retained_out) p.retained_out[(int64_t)b * p.scores_cap + j] = w;
+    if (!p.tier) continue;
+    if (w < n_tw_old) {
+      for (int i = 0; i < p.ppw; ++i) {
+        const int pg = tbl[w * p.ppw + i];
+        used[pg] = 1;
+        p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + i] = pg;
+      }
+    } else {
+      p.entrant[(int64_t)b * p.W + (w - n_tw_old)] = j;  // candidate -> new tier slot
+    }
+  }
+  for (int i = tid; i < p.local_w; i += nt) {
+    p.retained[(int64_t)b * p.R + k + i] = E + i;
+    if (p.retained_out) p.retained_out[(int64_t)b * p.scores_cap + k + i] = E + i;
+  }
+  if (!p.tier) return;
+  __syncthreads();
+  if (warp != 0) return;
+  // 4. entrants (at most 32 candidates) in chronological order take the
+  //    lowest free pages, ppw each
+  int e = 0;
+  {
+    const int w = n_tw_old + lane;
+    bool kept = lane < n_cand;
+    int j = 0;
+    if (kept) {
+      int before = 0;
+      for (int d = 0; d < m; ++d) {
+        before += s_drop[d] < w;
+        kept &= s_drop[d] != w;
+      }
+      j = w - before;
+    }
+    const unsigned km = __ballot_sync(0xffffffffu, kept);
+    if (kept) s_ent[__popc(km & ((1u << lane) - 1))] = j;
+    e = __popc(km);
+  }
+  const int need = e * p.ppw;  // <= 32 * 4
+  int found = 0;
+  for (int base = 0; base < p.page_cap && found < need; base += 32) {
+    const bool fr = base + lane < p.page_cap && !used[base + lane];
+    const unsigned fm = __ballot_sync(0xffffffffu, fr);
+    const int r = found + __popc(fm & ((1u << lane) - 1));
+    if (fr && r < need) s_free[r] = base + lane;
+    found += __popc(fm);
+  }
+  __syncwarp();
+  for (int x = lane; x < need; x += 32) {
+    const int r = x / p.ppw, i = x % p.ppw;
+    p.table_dst[(int64_t)b * p.page_cap + s_ent[r] * p.ppw + i] = s_free[x];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 2 (apply): one launch for everything that follows the selection.
 // Blocks [0, n_demote) quantise entrant windows into int4 pages, blocks
@@ -661,10 +808,20 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
 
 template <typename T>
 int launch_evict(EvictParams& p, cudaStream_t stream) {
-  const size_t smem = select_smem_bytes(p.E, p.R, p.tier ? p.page_cap : 0);
-  if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
-  cudaFuncSetAttribute(evict_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  evict_select_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
+  const int n_cand = p.E - p.n_tier_old_tok / p.ws;
+  const int m = p.E - p.kprime;
+  if (p.kprime > 0 && m > 0 && m <= kDropMax && (!p.tier || (n_cand <= 32 && p.ppw <= 4))) {
+    const size_t smem = (size_t)4 * p.E + 4 * ((size_t)(p.n_tier_old_tok / p.ws) * p.ppw + 1) +
+                        (p.tier ? (size_t)p.page_cap : 0) + 16;
+    if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
+    cudaFuncSetAttribute(evict_select_drop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    evict_select_drop_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
+  } else {
+    const size_t smem = select_smem_bytes(p.E, p.R, p.tier ? p.page_cap : 0);
+    if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
+    cudaFuncSetAttribute(evict_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    evict_select_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
+  }
   SKV_CHECK_LAUNCH();
   switch (p.D) {
     case 16: return launch_apply<T, 16>(p, stream);
