@@ -240,7 +240,7 @@ int skv_decode_attention_append(const skv_layer_desc* L, int32_t T, int32_t tier
 
 size_t skv_evict_workspace_size(const skv_layer_desc* L, int32_t W) {
   if (!L || W < 0) return 0;
-  return align_up((size_t)L->batch * (W > 0 ? W : 1) * 4, 256) * 2;
+  return align_up((size_t)L->batch * (W > 0 ? W : 1) * 4, 256) * 3;  // retained, entrant, keys
 }
 
 int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* a,
@@ -284,9 +284,10 @@ int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_ev
   p.tier = tier; p.scores_cap = a->scores_capacity; p.page_cap = src->tier_page_capacity;
   p.fp_cap_src = src->fp_capacity; p.fp_cap_dst = dst->fp_capacity; p.dtype = src->kv_dtype;
   p.scores_src = a->scores_src; p.scores_dst = a->scores_dst; p.ids_src = a->ids_src; p.ids_dst = a->ids_dst;
-  const size_t half = skv_evict_workspace_size(src, a->num_windows) / 2;
+  const size_t third = skv_evict_workspace_size(src, a->num_windows) / 3;
   p.retained = (int32_t*)ws;
-  p.entrant = (int32_t*)((char*)ws + half);
+  p.entrant = (int32_t*)((char*)ws + third);
+  p.keys = (uint32_t*)((char*)ws + 2 * third);
   p.retained_out = a->retained_out;
   p.next_window_id = a->next_window_id;
   p.table_src = src->tier_table; p.table_dst = dst->tier_table; p.pages = src->tier_pages;

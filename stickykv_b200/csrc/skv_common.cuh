@@ -174,6 +174,7 @@ struct EvictParams {
   int64_t* ids_dst;
   int32_t* retained;   // [B][R] (workspace)
   int32_t* entrant;    // [B][kprime] source window or -1 (workspace)
+  uint32_t* keys;      // [B][E] orderable head-mean scores (workspace)
   int32_t* retained_out;
   int64_t next_window_id;
   const int32_t* table_src;

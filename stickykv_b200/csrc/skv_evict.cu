@@ -70,6 +70,30 @@ constexpr int kSelectThreads = 1024;
 // decode step adds at most two windows before the next eviction.
 constexpr int kTailWindows = 8;
 
+// Head-mean keys of the evictable windows (policy.py:112 window_scores.mean
+// over query heads; heads summed in order h = 0..Hq-1 in fp32, then divided),
+// as orderable bits: one thread per (row, window) over the whole GPU, so the
+// 32 heads' scores of a row stream in parallel rather than through the one
+// CTA that selects for the row.
+constexpr int kKeysThreads = 256;
+__global__ void __launch_bounds__(kKeysThreads) evict_keys_kernel(EvictParams p) {
+  grid_launch_dependents();  // the select kernel stages its page table meanwhile
+  const int b = blockIdx.y, w = blockIdx.x * kKeysThreads + threadIdx.x;
+  if (w >= p.E) return;
+  const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap + w;
+  float acc = 0.f;
+  int h = 0;
+  for (; h + 16 <= p.Hq; h += 16) {  // loads issued 16 at a time
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc = __fadd_rn(acc, v[i]);
+  }
+  for (; h < p.Hq; ++h) acc = __fadd_rn(acc, rowp[(int64_t)h * p.scores_cap]);
+  p.keys[(int64_t)b * p.E + w] = orderable(__fdiv_rn(acc, (float)p.Hq));
+}
+
 __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int b = blockIdx.x;
@@ -89,29 +113,9 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   // 1. head-mean keys over the evictable prefix (orderable float bits)
   uint32_t thr = 0;
   int krem = 0;  // keys equal to thr that are kept, lowest window index first
+  grid_dependency_wait();  // the head-mean keys (evict_keys_kernel)
   if (partial) {
-    const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
-    for (int w = tid; w < E; w += nt) {
-      // heads summed in order; loads issued 32 at a time
-      float acc = 0.f;
-      int h = 0;
-      for (; h + 32 <= p.Hq; h += 32) {
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc = __fadd_rn(acc, v[i]);
-      }
-      for (; h + 16 <= p.Hq; h += 16) {
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc = __fadd_rn(acc, v[i]);
-      }
-      for (; h < p.Hq; ++h) acc = __fadd_rn(acc, rowp[(int64_t)h * p.scores_cap + w]);
-      keys[w] = orderable(__fdiv_rn(acc, (float)p.Hq));
-    }
+    for (int w = tid; w < E; w += nt) keys[w] = p.keys[(int64_t)b * E + w];
     if (tid == 0) s_krem = k;
     // 2. radix select of the k-th largest key, 8 bits per pass
     uint32_t prefix = 0, pmask = 0;
@@ -270,34 +274,15 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_drop_kernel(Evict
   __shared__ int s_ent[32];
   __shared__ int s_free[32 * 4];
 
-  // 1. head-mean keys (heads summed in order, as the radix path), the row's
-  //    logical tier page table, cleared page-use flags
-  const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
-  for (int w = tid; w < E; w += nt) {
-    float acc = 0.f;
-    int h = 0;
-    for (; h + 32 <= p.Hq; h += 32) {
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc = __fadd_rn(acc, v[i]);
-    }
-    for (; h + 16 <= p.Hq; h += 16) {
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap + w];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc = __fadd_rn(acc, v[i]);
-    }
-    for (; h < p.Hq; ++h) acc = __fadd_rn(acc, rowp[(int64_t)h * p.scores_cap + w]);
-    keys[w] = orderable(__fdiv_rn(acc, (float)p.Hq));
-  }
+  // 1. the row's logical tier page table and cleared page-use flags (before
+  //    the head-mean keys arrive), then the keys
   if (p.tier) {
     for (int i = tid; i < p.page_cap; i += nt) used[i] = 0;
     for (int i = tid; i < n_tw_old * p.ppw; i += nt) tbl[i] = p.table_src[(int64_t)b * p.page_cap + i];
     for (int c = tid; c < n_cand; c += nt) p.entrant[(int64_t)b * p.W + c] = -1;
   }
+  grid_dependency_wait();  // the head-mean keys (evict_keys_kernel)
+  for (int w = tid; w < E; w += nt) keys[w] = p.keys[(int64_t)b * E + w];
   __syncthreads();
   // 2. the m dropped windows, one block-wide argmin each
   for (int it = 0; it < m; ++it) {
@@ -810,19 +795,33 @@ template <typename T>
 int launch_evict(EvictParams& p, cudaStream_t stream) {
   const int n_cand = p.E - p.n_tier_old_tok / p.ws;
   const int m = p.E - p.kprime;
-  if (p.kprime > 0 && m > 0 && m <= kDropMax && (!p.tier || (n_cand <= 32 && p.ppw <= 4))) {
-    const size_t smem = (size_t)4 * p.E + 4 * ((size_t)(p.n_tier_old_tok / p.ws) * p.ppw + 1) +
-                        (p.tier ? (size_t)p.page_cap : 0) + 16;
-    if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
-    cudaFuncSetAttribute(evict_select_drop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    evict_select_drop_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
-  } else {
-    const size_t smem = select_smem_bytes(p.E, p.R, p.tier ? p.page_cap : 0);
-    if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
-    cudaFuncSetAttribute(evict_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    evict_select_kernel<<<p.B, kSelectThreads, smem, stream>>>(p);
+  const bool partial = p.kprime > 0 && m > 0;
+  const bool drop = partial && m <= kDropMax && (!p.tier || (n_cand <= 32 && p.ppw <= 4));
+  const size_t smem = drop ? (size_t)4 * p.E + 4 * ((size_t)(p.n_tier_old_tok / p.ws) * p.ppw + 1) +
+                                 (p.tier ? (size_t)p.page_cap : 0) + 16
+                           : select_smem_bytes(p.E, p.R, p.tier ? p.page_cap : 0);
+  if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
+  if (partial) {  // the selects read the keys only for a partial top-k
+    evict_keys_kernel<<<dim3(ceil_div(p.E, kKeysThreads), p.B), kKeysThreads, 0, stream>>>(p);
+    SKV_CHECK_LAUNCH();
   }
-  SKV_CHECK_LAUNCH();
+  auto kernel = drop ? evict_select_drop_kernel : evict_select_kernel;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.B);
+  cfg.blockDim = dim3(kSelectThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return SKV_ERR_CUDA;
+  }
   switch (p.D) {
     case 16: return launch_apply<T, 16>(p, stream);
     case 32: return launch_apply<T, 32>(p, stream);
