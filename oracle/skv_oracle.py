@@ -224,8 +224,35 @@ def rope_apply_kdtype(k: np.ndarray, cos: np.ndarray, sin: np.ndarray, dtype: st
     return round_to((t1 + t2).astype(np.float32), dtype)
 
 
+_POOL = None
+
+
+def _pool():
+    """Host threads for elementwise work on large arrays (numpy's ufuncs
+    release the GIL, so slices run in parallel; results are unchanged)."""
+    global _POOL
+    if _POOL is None:
+        import concurrent.futures
+        import os
+        _POOL = concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 1)
+    return _POOL
+
+
 def rerotate_keys(k: np.ndarray, old_pos: np.ndarray, new_pos: np.ndarray,
                   cos_tab: np.ndarray, sin_tab: np.ndarray, dtype: str) -> np.ndarray:
+    """Strip RoPE at ``old_pos`` then re-apply at ``new_pos`` (state.py:199-221);
+    see :func:`rerotate_keys_serial`.  Large caches are split over kv heads
+    and host threads (each head's arithmetic is independent)."""
+    B, H = k.shape[0], k.shape[1]
+    if k.size < (1 << 20) or H == 1:
+        return rerotate_keys_serial(k, old_pos, new_pos, cos_tab, sin_tab, dtype)
+    parts = list(_pool().map(lambda h: rerotate_keys_serial(k[:, h:h + 1], old_pos, new_pos, cos_tab,
+                                                            sin_tab, dtype), range(H)))
+    return np.concatenate(parts, axis=1)
+
+
+def rerotate_keys_serial(k: np.ndarray, old_pos: np.ndarray, new_pos: np.ndarray,
+                         cos_tab: np.ndarray, sin_tab: np.ndarray, dtype: str) -> np.ndarray:
     """Strip RoPE at ``old_pos`` then re-apply at ``new_pos`` (state.py:199-221).
 
     ``k`` [B,H,T,D] (values representable in ``dtype``), positions [B,T].

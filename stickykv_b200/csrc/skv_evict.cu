@@ -487,6 +487,7 @@ struct ApplyGrid {
   int demote_tasks;   // (candidate window, page) pairs per (row, kv head)
   int gather_chunks;  // kApplyThreads-window chunks per row
   int move_chunks;    // token chunks per row
+  int k_hsplit;       // kv-head slices of the key move (more threads when few rows)
   int n_fp_tok;       // fp tokens that stay fp, per row
 };
 
@@ -550,7 +551,10 @@ template <typename T, int D>
 __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) {
   constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr int half = D / 2, nvec = half / VE, tpb = kApplyThreads / nvec;
+  const int hs = bid % a.k_hsplit;  // this block's slice of the kv heads
+  bid /= a.k_hsplit;
   const int b = bid / a.move_chunks, chunk = bid % a.move_chunks;
+  const int h_begin = hs * p.Hkv / a.k_hsplit, h_end = (hs + 1) * p.Hkv / a.k_hsplit;
   const int tau = chunk * tpb + threadIdx.x / nvec, c0 = (threadIdx.x % nvec) * VE;
   if (threadIdx.x >= tpb * nvec || tau >= a.n_fp_tok) return;
   const int s_eff = min(p.s, p.T_old);
@@ -595,17 +599,17 @@ __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) 
     const T* ks0 = (const T*)p.k_src + ((int64_t)b * p.Hkv * p.fp_cap_src + so_slot) * D + c0;
     T* kd0 = (T*)p.k_dst + ((int64_t)b * p.Hkv * p.fp_cap_dst + sd_slot) * D + c0;
 #pragma unroll 1
-    for (int h0 = 0; h0 < p.Hkv; h0 += HB) {
+    for (int h0 = h_begin; h0 < h_end; h0 += HB) {
       V2 x[HB], y[HB];
 #pragma unroll
       for (int j = 0; j < HB; ++j)
-        if (h0 + j < p.Hkv) {
+        if (h0 + j < h_end) {
           x[j].u = *reinterpret_cast<const uint4*>(ks0 + (h0 + j) * hs_src);
           y[j].u = *reinterpret_cast<const uint4*>(ks0 + (h0 + j) * hs_src + half);
         }
 #pragma unroll
       for (int j = 0; j < HB; ++j) {
-        if (h0 + j >= p.Hkv) break;
+        if (h0 + j >= h_end) break;
 #pragma unroll
         for (int e = 0; e < VE / 2; ++e) {
           // strip (cos, -sin), then re-apply (cos, sin)
@@ -629,7 +633,7 @@ __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) 
     }
     union Vec { uint4 u; T e[VE]; };
 #pragma unroll 1
-    for (int h = 0; h < p.Hkv; ++h) {
+    for (int h = h_begin; h < h_end; ++h) {
       const T* ks = (const T*)p.k_src + (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
       T* kd = (T*)p.k_dst + (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
       Vec kx, ky, ox, oy;
@@ -762,7 +766,10 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
   a.n_fp_tok = p.T_new - p.n_tier_new_tok;  // sinks + fp windows kept
   constexpr int tpb = kApplyThreads / (D / 2 / (16 / (int)sizeof(T)));
   a.move_chunks = a.n_fp_tok > 0 ? ceil_div(a.n_fp_tok, tpb) : 0;
-  a.n_move = a.move_chunks * p.B;
+  // few rows: slice the kv heads over blocks so each thread keeps one round of
+  // loads in flight instead of walking all heads (4 heads per slice)
+  a.k_hsplit = (a.move_chunks * p.B < 2 * 148) ? max(1, p.Hkv / 4) : 1;
+  a.n_move = a.move_chunks * p.B * a.k_hsplit;
   {
     const int s_eff = min(p.s, p.T_old);
     const int rest = a.n_fp_tok > s_eff ? a.n_fp_tok - s_eff : 0;
