@@ -521,6 +521,8 @@ def run_e2e(args, rank, world, dev):
     torch.manual_seed(1234 + rank)
     with torch.device(dev):
         model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    if args.e2e_stock:
+        return run_stock_e2e(args, rank, world, dev, model, c, rows)
     wcfg = WindowedCacheConfig(window_size=WS, num_sink_tokens=SINKS, local_window_size=LOCAL,
                                cache_budget=budget, int4_tier=True)
     torch.cuda.reset_peak_memory_stats(dev)
@@ -613,6 +615,54 @@ def run_e2e(args, rank, world, dev):
                    f"{n_eager} eager steps that reach it)") if used_graphs else "eager",
         "nccl_ranks": world if world > 1 else None,
         "peak_mem_gib": peak / 2 ** 30, "clocks": clocks,
+    }
+
+
+def run_stock_e2e(args, rank, world, dev, model, c, rows):
+    """The same model, rows and prompt through stock transformers: its own
+    DynamicCache (every token kept, no eviction) and sdpa attention, decoded
+    eagerly (a growing cache has no steady state to replay).  The comparison
+    point a user of plain transformers gets: TTFT, TPOT, decode tokens/s and
+    peak device memory."""
+    import torch
+    import torch.distributed as dist
+    from transformers import DynamicCache
+    model.config._attn_implementation = "sdpa"
+    g = torch.Generator(device=dev).manual_seed(55 + rank)
+    ids = torch.randint(0, c["vocab"], (rows, c["prompt"]), device=dev, generator=g)
+    torch.cuda.reset_peak_memory_stats(dev)
+    stream = torch.cuda.current_stream(dev)
+    cache = DynamicCache()
+    with torch.no_grad():
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        p1.record(stream)
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = c["decode"] - 1
+        t0.record(stream)
+        for _ in range(steps):
+            out = model(input_ids=nxt, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    dec_ms, pre_ms, peak = max_over_ranks(
+        [t0.elapsed_time(t1), p0.elapsed_time(p1), torch.cuda.max_memory_allocated(dev)], dev, world)
+    if rank != 0:
+        return None
+    return {
+        "metric": "e2e decode tokens/s, stock transformers (DynamicCache, sdpa, no eviction)", "unit": "tokens/s",
+        "value": rows * world * steps / (dec_ms * 1e-3), "n_gpus": world, "steps": steps,
+        "ms_per_step": dec_ms / steps, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+        "data": "synthetic: random N(0,0.02) weights, uniform token ids",
+        "config": {"workload": "Llama-3.2-1B-shaped decoder, greedy decode through stock transformers",
+                   "global_batch": rows * world, "prompt": c["prompt"], "decode_steps": c["decode"],
+                   "retained_tokens": cache.get_seq_length(0)},
+        "prefill_ms": pre_ms, "ttft_ms": pre_ms, "tpot_ms": dec_ms / steps, "peak_mem_gib": peak / 2 ** 30,
     }
 
 
@@ -775,6 +825,8 @@ def main():
     ap.add_argument("--e2e-prompt", type=int, default=0)
     ap.add_argument("--e2e-decode", type=int, default=0)
     ap.add_argument("--e2e-budget", type=float, default=0.0)
+    ap.add_argument("--e2e-stock", action="store_true",
+                    help="with --e2e: the same model through stock transformers (DynamicCache, sdpa, no eviction)")
     ap.add_argument("--e2e-eager", action="store_true",
                     help="decode the model run eagerly (no CUDA-graph replay of its steps)")
     ap.add_argument("--rows", type=int, default=0,
