@@ -94,6 +94,24 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
 
 
+class _no_gc:
+    """Collect now, then keep Python's cyclic collector out of a timed region
+    (in a process with transformers loaded one full collection takes tens of
+    milliseconds, which would land in a host-driven step)."""
+
+    def __enter__(self):
+        import gc
+        gc.collect()
+        self.was = gc.isenabled()
+        gc.disable()
+
+    def __exit__(self, *exc):
+        import gc
+        if self.was:
+            gc.enable()
+        return False
+
+
 def max_over_ranks(values, dev, world):
     """Element-wise max of per-rank timings over all ranks (every rank gets
     the result; the job is as slow as its slowest rank)."""
@@ -315,10 +333,11 @@ def run_ours(args, rank, world, dev):
             dist.barrier()
         torch.cuda.synchronize(dev)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        graphs.replay(args.steps)
-        t1.record(stream)
-        torch.cuda.synchronize(dev)
+        with _no_gc():
+            t0.record(stream)
+            graphs.replay(args.steps)
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         clocks = sampler.stop()
@@ -359,13 +378,14 @@ def run_ours(args, rank, world, dev):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(cstream)
-    for i in range(args.steps):
-        e2e_step(i)
-    cstream.wait_stream(copy_stream)
-    e1.record(cstream)
-    torch.cuda.synchronize(dev)
+    with _no_gc():  # a full collection in this process takes tens of ms: not in the timed steps
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cstream)
+        for i in range(args.steps):
+            e2e_step(i)
+        cstream.wait_stream(copy_stream)
+        e1.record(cstream)
+        torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
     h2d = din.numel() * 2
     d2h = hout[0].numel() * 2
@@ -577,14 +597,15 @@ def run_e2e(args, rank, world, dev):
             dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         n_timed = total - n_eager
-        t0.record(stream)
-        if graphs is not None:
-            graphs.replay(n_timed)
-        else:
-            for _ in range(n_timed):
-                decode_step()
-        t1.record(stream)
-        torch.cuda.synchronize(dev)
+        with _no_gc():
+            t0.record(stream)
+            if graphs is not None:
+                graphs.replay(n_timed)
+            else:
+                for _ in range(n_timed):
+                    decode_step()
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         clocks = sampler.stop()

@@ -32,8 +32,12 @@
 //       to the page start R(-P) q (and pre-scaled into the log2 domain) for
 //       int4 pages, whose keys are stored in their page frame.  The rotated
 //       query steps R(-16) from one tile to the next (packed f32x2 math).
-//       int4 codes are expanded by magic-number OR into fp16 and dequantised
-//       with one packed FMA per two channels, straight into A fragments.
+//       int4 K codes enter the MMA raw, masked into exact fp16 subnormals
+//       (per-group accumulators; each token's scale and zero point are
+//       applied to its score afterwards, the zero point through the group
+//       sums of the query from one more MMA); int4 V codes are expanded by
+//       magic-number OR into fp16 and dequantised with one packed FMA per two
+//       channels, straight into A fragments.
 //   softmax in the log2 domain, online per warp with lazy rescaling; the
 //       window mass of each unit is the sum of its 8 rows.
 //   PV  mma: O^T = V^T P, V^T fragments via ldmatrix.trans (fp) or
@@ -284,8 +288,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   float rq[KB][4];
   int rq_pos = -1;
   const bool can_step = p.rope_rows > kRotStep;
-  // rq = scl * R(-P) q
-  auto seed = [&](int P, float scl) {
+  // rq = scl * R(-P) q; with `raw` the elements e >= 2 (k-rows 8..15 of each
+  // k-block, which meet the odd nibbles of the raw int4 codes, 16x larger)
+  // carry an extra 1/16 (exact: a power of two)
+  auto seed = [&](int P, float scl, bool raw) {
 #pragma unroll
     for (int kb = 0; kb < KB / 2; ++kb)
 #pragma unroll
@@ -293,10 +299,12 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
         const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
         const float c = p.cos[(int64_t)P * (D / 2) + d], s = p.sin[(int64_t)P * (D / 2) + d];
         const float x = q_live ? ld_f32(qp + d) : 0.f, y = q_live ? ld_f32(qp + d + D / 2) : 0.f;
-        rq[kb][e] = fmaf(x, c, y * s) * scl;
-        rq[kb + KB / 2][e] = fmaf(y, c, -x * s) * scl;
+        const float f = (raw && e >= 2) ? scl * 0.0625f : scl;
+        rq[kb][e] = fmaf(x, c, y * s) * f;
+        rq[kb + KB / 2][e] = fmaf(y, c, -x * s) * f;
       }
   };
+
   auto load_qb = [&](uint32_t (&qb)[KB][2]) {
 #pragma unroll
     for (int kb = 0; kb < KB; ++kb) {
@@ -342,12 +350,29 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
     }
   };
 
+  // raw K codes of an int4 page: the nibbles masked in place, each an exact
+  // fp16 subnormal c * 2^-24 (even nibbles, A columns 2t..) or c * 2^-20 (odd
+  // nibbles, columns 2t+8..; the query rows they meet carry 1/16), one logic
+  // op per two codes; the scale and zero point are applied after the MMA.
+  // (V codes are dequantised into A fragments: a scale folded into P plus
+  // MMAs for the offsets and zero points measured slower.)
+  auto page_k_raw = [&](uint32_t pg, uint32_t (&ka)[KB][2]) {
+    const Words<NW> w = lds_words<NW>(pg + kc_off);
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+      const uint32_t lo = w.w[q], hi = w.w[q] >> 8;
+      ka[2 * q][0] = lo & 0x000F000Fu;
+      ka[2 * q][1] = lo & 0x00F000F0u;
+      ka[2 * q + 1][0] = hi & 0x000F000Fu;
+      ka[2 * q + 1][1] = hi & 0x00F000F0u;
+    }
+  };
+
   // ---- softmax (log2 domain) with lazy rescale, PV, window mass ----
   // sc0/sc1: this thread's two scores (row g of its unit, heads hh0, hh0+1),
   // -inf where the row holds no token.  kFp16P: P packed as fp16 for both
   // units (int4 tile, or bf16 cache tile whose units are all int4).
-  auto softmax_pv = [&](float sc0, float sc1, bool guard, uint32_t (&va)[2][KB][2], int mode_pv,
-                        int clsA, int clsB, int i) {
+  auto softmax_p = [&](float sc0, float sc1, bool guard, float& pr0, float& pr1) {
     if (__any_sync(0xffffffffu, sc0 > m_thr[0] || sc1 > m_thr[1])) {
       float mx0 = sc0, mx1 = sc1;
 #pragma unroll
@@ -370,14 +395,33 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       m_thr[0] = mn0 + kThresh;
       m_thr[1] = mn1 + kThresh;
     }
-    float pr0 = ex2(sc0 - m_run[0]);
-    float pr1 = ex2(sc1 - m_run[1]);
+    pr0 = ex2(sc0 - m_run[0]);
+    pr1 = ex2(sc1 - m_run[1]);
     if (guard) {  // rows without a token (and nothing seen yet)
       pr0 = sc0 == -INFINITY ? 0.f : pr0;
       pr1 = sc1 == -INFINITY ? 0.f : pr1;
     }
     l_run[0] += pr0;
     l_run[1] += pr1;
+  };
+  // ---- window mass: sum of the unit's 8 rows per head (exact fp32) ----
+  auto store_mass = [&](float pr0, float pr1, int i) {
+    // lanes g, g^1 swap one head each, then reduce over the remaining g bits
+    float a = (g & 1) ? pr1 : pr0;
+    const float other = (g & 1) ? pr0 : pr1;
+    a += __shfl_xor_sync(0xffffffffu, other, 4);
+    a += __shfl_xor_sync(0xffffffffu, a, 8);
+    a += __shfl_xor_sync(0xffffffffu, a, 16);
+    if (lane < 8) {  // g in {0,1}: head hh0 + g of unit t>>1
+      float* ms = mass_s + i * 12;
+      ms[my_unit * 4 + hh0 + g] = a;
+      if (lane < 2) *reinterpret_cast<float2*>(ms + 8 + hh0) = make_float2(m_run[0], m_run[1]);
+    }
+  };
+  auto softmax_pv = [&](float sc0, float sc1, bool guard, uint32_t (&va)[2][KB][2], int mode_pv,
+                        int clsA, int clsB, int i) {
+    float pr0, pr1;
+    softmax_p(sc0, sc1, guard, pr0, pr1);
     // ---- O^T += V^T P ----
     if (mode_pv == 1) {  // one operand type for both units
       const uint32_t pk = H::pack(pr0, pr1);
@@ -404,18 +448,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
                pb0 & ~n0, pb1 & ~n1);
       }
     }
-    // ---- window mass: sum of the unit's 8 rows per head (exact fp32) ----
-    // lanes g, g^1 swap one head each, then reduce over the remaining g bits
-    float a = (g & 1) ? pr1 : pr0;
-    const float other = (g & 1) ? pr0 : pr1;
-    a += __shfl_xor_sync(0xffffffffu, other, 4);
-    a += __shfl_xor_sync(0xffffffffu, a, 8);
-    a += __shfl_xor_sync(0xffffffffu, a, 16);
-    if (lane < 8) {  // g in {0,1}: head hh0 + g of unit t>>1
-      float* ms = mass_s + i * 12;
-      ms[my_unit * 4 + hh0 + g] = a;
-      if (lane < 2) *reinterpret_cast<float2*>(ms + 8 + hh0) = make_float2(m_run[0], m_run[1]);
-    }
+    store_mass(pr0, pr1, i);
   };
 
   // ======================= int4 tiles (both units pages) =======================
@@ -458,12 +491,12 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
     // query of this thread's column at the first tile
     {
       const int P = p.s + 8 * (u0 + 2 * i0 - R.NS + (g >> 2));
-      if (P != rq_pos) seed(P, p.scale_log2);
+      if (P != rq_pos) seed(P, p.scale_log2, true);
     }
     uint32_t cs = ring_s, is = ring_s + (SL - 1) * SB;
 #pragma unroll 2
     for (int i = i0; i < i1; ++i) {
-      if (!can_step && i > i0) seed(p.s + 8 * (u0 + 2 * i - R.NS + (g >> 2)), p.scale_log2);
+      if (!can_step && i > i0) seed(p.s + 8 * (u0 + 2 * i - R.NS + (g >> 2)), p.scale_log2, true);
       if (i + SL - 1 < i1) issue(i + SL - 1, is + lane * 16);
       cp_commit();
       is = is + SB == ring_s + SL * SB ? ring_s : is + SB;
@@ -488,18 +521,38 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       cp_wait<SL - 1>();
       __syncwarp();
       uint32_t ka[2][KB][2], va[2][KB][2];
-      page_k(cs, ka[0]);
-      page_k(cs + PB, ka[1]);
-      float sacc[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+      page_k_raw(cs, ka[0]);
+      page_k_raw(cs + PB, ka[1]);
+      // per group: acc = 2^-24 sum_d c q (the raw codes), qs = sum_d q (the
+      // zero points' factor, from a constant A of ones, 16 on the columns
+      // that meet the 1/16-scaled query elements); this thread's two scores
+      // (row g of its unit, heads hh0, hh0 + 1) are the sums over groups of
+      // s * 2^24 acc + z * qs, s and z of the token's group
+      float acc[NW][4], qs[NW][4];
 #pragma unroll
-      for (int kb = 0; kb < KB; ++kb)
-        H::mma((kb & 1) ? s2 : sacc, ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+      for (int gq = 0; gq < NW; ++gq)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[gq][c] = qs[gq][c] = 0.f;
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) {
+        H::mma(acc[kb >> 1], ka[0][kb][0], ka[1][kb][0], ka[0][kb][1], ka[1][kb][1], qB[kb][0], qB[kb][1]);
+        H::mma(qs[kb >> 1], 0x3C003C00u, 0x3C003C00u, 0x4C004C00u, 0x4C004C00u, qB[kb][0], qB[kb][1]);
+      }
+      const Words<NW> ksz = lds_words<NW>(cs + (my_unit ? PB : 0) + ks_off);
       page_v(cs, va[0]);
       page_v(cs + PB, va[1]);
       __syncwarp();
       cs = cs + SB == ring_s + SL * SB ? ring_s : cs + SB;
-      const float sc0 = my_unit ? sacc[2] + s2[2] : sacc[0] + s2[0];
-      const float sc1 = my_unit ? sacc[3] + s2[3] : sacc[1] + s2[1];
+      float t0 = 0.f, t1 = 0.f, z0 = 0.f, z1 = 0.f;
+#pragma unroll
+      for (int gq = 0; gq < NW; ++gq) {
+        const float2 sz = __half22float2(h2(ksz.w[gq]));
+        t0 = fmaf(sz.x, my_unit ? acc[gq][2] : acc[gq][0], t0);
+        t1 = fmaf(sz.x, my_unit ? acc[gq][3] : acc[gq][1], t1);
+        z0 = fmaf(sz.y, qs[gq][0], z0);
+        z1 = fmaf(sz.y, qs[gq][1], z1);
+      }
+      const float sc0 = fmaf(0x1p24f, t0, z0), sc1 = fmaf(0x1p24f, t1, z1);
       softmax_pv(sc0, sc1, false, va, 1, 1, 1, i);
     }
     rq_pos = can_step ? p.s + 8 * (u0 + 2 * i1 - R.NS + (g >> 2)) : -1;
@@ -606,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
       const int my_kind = (g >> 2) ? kB : kA;
       uint32_t qB[KB][2];
       if (my_kind == 2) {
-        seed(p.s + 8 * ((ua + (g >> 2)) - R.NS), 1.f);
+        seed(p.s + 8 * ((ua + (g >> 2)) - R.NS), 1.f, false);
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb) {
           qB[kb][0] = H::pack(rq[kb][0], rq[kb][1]);
