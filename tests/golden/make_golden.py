@@ -29,11 +29,17 @@ Fixtures:
   cfg1_e2e_<dt>.npz    the same model cast to fp16 / bf16: teacher-forced on
                        the fp32 tokens (logits, window ids, scores) and
                        free-running greedy (tokens, top-2 margins)
+  cfg1_runner.npz      the parity runner's per-step capture on the fp32 cfg1
+                       model, teacher-forced: eviction flags, effective window
+                       scores and ids per layer, and the runner's
+                       _extract_row_retained of them (ragged arrays stored
+                       flat with per-step shapes)
 """
 
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -243,12 +249,13 @@ def gen_prefill_scores(scorer):
                         scores=to_np(sc))
 
 
-def gen_cfg1_e2e(ref_eager):
-    """Reference eager backend on the cfg1 model.  transformers 5.5 needs a
-    harness shim that changes no reference arithmetic: the Cache mask-size API
-    (``layers``, ``is_compileable``, ``get_mask_sizes``) and an eager attention
-    wrapper that trims the mask to the compacted key length (the 4.47
-    behaviour)."""
+@contextlib.contextmanager
+def _cfg1_env(ref_eager):
+    """The cfg1 model's module and the transformers 5.5 harness shim around
+    the reference eager backend.  The shim changes no reference arithmetic:
+    the Cache mask-size API (``layers``, ``is_compileable``,
+    ``get_mask_sizes``) and an eager attention wrapper that trims the mask to
+    the compacted key length (the 4.47 behaviour)."""
     import transformers.models.llama.modeling_llama as LM
     import importlib.util
     spec = importlib.util.spec_from_file_location("skv_cfg1", os.path.join(os.path.dirname(HERE), "_cfg1.py"))
@@ -272,17 +279,26 @@ def gen_cfg1_e2e(ref_eager):
 
     LM.eager_attention_forward = eager_trimmed
     try:
-        model = C1.build_model()
-        wcfg = ref_eager.WindowedCacheConfig(window_size=C1.WINDOW, num_sink_tokens=C1.SINKS,
-                                             local_window_size=C1.LOCAL, cache_budget=C1.BUDGET)
-        cache = Shim(config=wcfg, prefill_len=C1.PROMPT_LEN, model_config=model.config,
-                     kv_dtype=torch.float32, rope_module=model.model.rotary_emb,
-                     num_layers=2, max_tokens=C1.STEPS)
-        handles = ref_eager.install_score_hooks(model, cache, wcfg)
-        toks, top_i, top_v = C1.greedy(model, cache, C1.prompt(), output_attentions=True)
-        handles.remove()
+        yield C1, Shim
     finally:
         LM.eager_attention_forward = eager
+
+
+def _cfg1_cache(ref_eager, C1, Shim, model, dt):
+    wcfg = ref_eager.WindowedCacheConfig(window_size=C1.WINDOW, num_sink_tokens=C1.SINKS,
+                                         local_window_size=C1.LOCAL, cache_budget=C1.BUDGET)
+    cache = Shim(config=wcfg, prefill_len=C1.PROMPT_LEN, model_config=model.config, kv_dtype=dt,
+                 rope_module=model.model.rotary_emb, num_layers=2, max_tokens=C1.STEPS)
+    return cache, ref_eager.install_score_hooks(model, cache, wcfg)
+
+
+def gen_cfg1_e2e(ref_eager):
+    """Reference eager backend on the cfg1 model (harness: :func:`_cfg1_env`)."""
+    with _cfg1_env(ref_eager) as (C1, Shim):
+        model = C1.build_model()
+        cache, handles = _cfg1_cache(ref_eager, C1, Shim, model, torch.float32)
+        toks, top_i, top_v = C1.greedy(model, cache, C1.prompt(), output_attentions=True)
+        handles.remove()
     rec = dict(tokens=np.array(toks, np.int64), top_i=top_i.astype(np.int64), top_v=top_v.astype(np.float32),
                seq_len=np.array(cache.get_seq_length(0)))
     for li in range(2):
@@ -296,47 +312,19 @@ def gen_cfg1_e2e(ref_eager):
 
 def gen_cfg1_e2e_half(ref_eager):
     """The cfg1 model cast to fp16 and to bf16 through the reference's eager
-    backend (same harness shim as :func:`gen_cfg1_e2e`; matmuls accumulate in
-    fp32, the softmax runs in fp32 and is cast to the model dtype, window
-    scores accumulate in the model dtype).  Two runs per dtype:
-    teacher-forced on the fp32 run's greedy tokens (top-64 logits per step,
-    final per-layer window ids, scores, the last step's pending scores, seq
-    length) and free-running greedy (tokens and the top-1/top-2 logit margin
-    of every step)."""
-    import transformers.models.llama.modeling_llama as LM
-    import importlib.util
-    spec = importlib.util.spec_from_file_location("skv_cfg1", os.path.join(os.path.dirname(HERE), "_cfg1.py"))
-    C1 = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(C1)
+    backend (harness: :func:`_cfg1_env`; matmuls accumulate in fp32, the
+    softmax runs in fp32 and is cast to the model dtype, window scores
+    accumulate in the model dtype).  Two runs per dtype: teacher-forced on the
+    fp32 run's greedy tokens (top-64 logits per step, final per-layer window
+    ids, scores, the last step's pending scores, seq length) and free-running
+    greedy (tokens and the top-1/top-2 logit margin of every step)."""
     fp32 = np.load(os.path.join(HERE, "cfg1_e2e.npz"))
-
-    class Shim(ref_eager.WindowedCache):
-        layers = []
-        is_compileable = False
-
-        def get_mask_sizes(self, q_len, layer_idx=0):
-            q = int(q_len.shape[0]) if torch.is_tensor(q_len) else int(q_len)
-            return self.get_seq_length(layer_idx) + q, 0
-
-    eager = LM.eager_attention_forward
-
-    def eager_trimmed(module, q, k, v, mask, *a, **kw):
-        if mask is not None:
-            mask = mask[..., : k.shape[-2]]
-        return eager(module, q, k, v, mask, *a, **kw)
-
-    LM.eager_attention_forward = eager_trimmed
-    try:
+    with _cfg1_env(ref_eager) as (C1, Shim):
         for name, dt in (("f16", torch.float16), ("bf16", torch.bfloat16)):
             rec = {"tf_tokens": fp32["tokens"]}
             for mode in ("tf", "greedy"):
                 model = C1.build_model().to(dt)
-                wcfg = ref_eager.WindowedCacheConfig(window_size=C1.WINDOW, num_sink_tokens=C1.SINKS,
-                                                     local_window_size=C1.LOCAL, cache_budget=C1.BUDGET)
-                cache = Shim(config=wcfg, prefill_len=C1.PROMPT_LEN, model_config=model.config,
-                             kv_dtype=dt, rope_module=model.model.rotary_emb, num_layers=2,
-                             max_tokens=C1.STEPS)
-                handles = ref_eager.install_score_hooks(model, cache, wcfg)
+                cache, handles = _cfg1_cache(ref_eager, C1, Shim, model, dt)
                 if mode == "tf":
                     top_i, top_v = C1.teacher_forced(model, cache, C1.prompt(), fp32["tokens"],
                                                      output_attentions=True)
@@ -353,8 +341,68 @@ def gen_cfg1_e2e_half(ref_eager):
                                greedy_margin=(top_v[:, 0] - top_v[:, 1]).astype(np.float32))
                 handles.remove()
             np.savez_compressed(os.path.join(HERE, f"cfg1_e2e_{name}.npz"), **rec)
-    finally:
-        LM.eager_attention_forward = eager
+
+
+def _effective_scores(cache, li):
+    """[1, H, W] window scores of layer ``li`` including the step's scores
+    that the reference keeps pending in ``cache_kwargs`` until the next
+    update(), and the [1, W] original window ids (identity before the first
+    eviction)."""
+    st = cache._states[li]
+    pend = cache.cache_kwargs[li].get("window_scores") if li in cache.cache_kwargs else None
+    ids = st.original_window_ids
+    W = ids.shape[-1] if ids is not None else max(
+        st.window_scores.shape[-1] if st.window_scores is not None else 0,
+        pend.shape[-1] if pend is not None else 0)
+    if ids is None:
+        ids = torch.arange(W, dtype=torch.long).unsqueeze(0)
+    H = (st.window_scores if st.window_scores is not None else pend).shape[1]
+    eff = torch.zeros(1, H, W, dtype=torch.float32)
+    for part in (st.window_scores, pend):
+        if part is not None:
+            n = min(W, part.shape[-1])
+            eff[..., :n] += part[..., :n].float()
+    return eff, ids.long()
+
+
+def gen_cfg1_runner(ref_eager, extract_row_retained):
+    """The parity runner's per-step capture (modules/evaluation/
+    ours_parity_runner.py:312-402) on the fp32 cfg1 model through the
+    reference eager backend, teacher-forced on the fp32 greedy tokens: per
+    step the eviction flag, and per layer the effective window scores, the
+    original window ids and the runner's own ``_extract_row_retained`` of
+    them (its top-K window ids, fp16 scores, retained ids and retained fp16
+    scores)."""
+    fp32 = np.load(os.path.join(HERE, "cfg1_e2e.npz"))
+    with _cfg1_env(ref_eager) as (C1, Shim):
+        model = C1.build_model()
+        cache, handles = _cfg1_cache(ref_eager, C1, Shim, model, torch.float32)
+        tk = cache.resolved.top_k_windows
+        rec = {"tokens": fp32["tokens"], "top_k": np.array(tk)}
+        steps = {k: [] for k in ("evicted", "W")}
+        per = {}
+        inp = C1.prompt()
+        with torch.no_grad():
+            for step in range(C1.STEPS):
+                model(input_ids=inp, past_key_values=cache, use_cache=True, return_dict=True,
+                      output_attentions=True)
+                gs = cache._generation_step
+                steps["evicted"].append(any((gs[li] - 1) > 0 and (gs[li] - 1) % C1.WINDOW == 0 for li in range(2)))
+                for li in range(2):
+                    eff, ids = _effective_scores(cache, li)
+                    a_tk, a_ws, a_rid, a_rsc = extract_row_retained(eff[0], ids[0], tk, C1.WINDOW, C1.LOCAL)
+                    for key, val in (("scores", eff[0].numpy()), ("ids", ids[0].numpy()), ("tk", a_tk),
+                                     ("ws16", a_ws), ("ret_ids", a_rid), ("ret_sc16", a_rsc)):
+                        per.setdefault(f"{key}_{li}", []).append(val)
+                if step + 1 < C1.STEPS:
+                    inp = torch.tensor([[int(fp32["tokens"][step])]])
+        handles.remove()
+    rec["evicted"] = np.array(steps["evicted"], bool)
+    for key, vals in per.items():  # ragged over steps: concatenated with per-step lengths
+        rec[key] = np.concatenate([np.asarray(v).reshape(-1) for v in vals])
+        rec[key + "_shape"] = np.array([np.asarray(v).shape + (0,) * (2 - np.asarray(v).ndim) for v in vals],
+                                       np.int64)
+    np.savez_compressed(os.path.join(HERE, "cfg1_runner.npz"), **rec)
 
 
 def main():
@@ -378,6 +426,8 @@ def main():
     import modules.windowed_eager_cache as ref_eager
     gen_cfg1_e2e(ref_eager)
     gen_cfg1_e2e_half(ref_eager)
+    from modules.evaluation.ours_parity_runner import _extract_row_retained
+    gen_cfg1_runner(ref_eager, _extract_row_retained)
     print("golden fixtures written to", HERE)
 
 
