@@ -250,16 +250,17 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
 // m = E - k smallest keys taken in (key ascending, index descending) order,
 // so m block-wide argmin passes find the dropped windows, every kept window's
 // chronological slot is its index minus the dropped windows before it, and
-// with the int4 tier the few entrants take the lowest free pages found by
-// warp ballots.  Used when m <= kDropMax and (with the tier) at most 32
-// candidate windows can enter the tier.
+// with the int4 tier the few entrants take the lowest free pages, ranked by
+// one block scan over the pool.  Used when m <= kDropMax and (with the
+// tier) at most 32 candidate windows can enter the tier.
 constexpr int kDropMax = 8;
+constexpr int kDropThreads = 1024;
 
 __device__ __forceinline__ uint64_t drop_order(uint32_t key, int w) {
   return ((uint64_t)key << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)w);  // min: key asc, index desc
 }
 
-__global__ void __launch_bounds__(kSelectThreads) evict_select_drop_kernel(EvictParams p) {
+__global__ void __launch_bounds__(kDropThreads) evict_select_drop_kernel(EvictParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int b = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
@@ -273,6 +274,8 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_drop_kernel(Evict
   __shared__ int s_drop[kDropMax];
   __shared__ int s_ent[32];
   __shared__ int s_free[32 * 4];
+  __shared__ int s_scan[32];
+  __shared__ int s_need;
 
   // 1. the row's logical tier page table and cleared page-use flags (before
   //    the head-mean keys arrive), then the keys
@@ -334,12 +337,11 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_drop_kernel(Evict
     if (p.retained_out) p.retained_out[(int64_t)b * p.scores_cap + k + i] = E + i;
   }
   if (!p.tier) return;
-  __syncthreads();
-  if (warp != 0) return;
   // 4. entrants (at most 32 candidates) in chronological order take the
-  //    lowest free pages, ppw each
-  int e = 0;
-  {
+  //    lowest free pages, ppw each: warp 0 ranks the entrants while every
+  //    thread counts the free pages of its slice of the pool, and one block
+  //    scan ranks the free pages
+  if (warp == 0) {
     const int w = n_tw_old + lane;
     bool kept = lane < n_cand;
     int j = 0;
@@ -353,21 +355,22 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_drop_kernel(Evict
     }
     const unsigned km = __ballot_sync(0xffffffffu, kept);
     if (kept) s_ent[__popc(km & ((1u << lane) - 1))] = j;
-    e = __popc(km);
+    if (lane == 0) s_need = __popc(km) * p.ppw;  // <= 32 * 4
   }
-  const int need = e * p.ppw;  // <= 32 * 4
-  int found = 0;
-  for (int base = 0; base < p.page_cap && found < need; base += 32) {
-    const bool fr = base + lane < p.page_cap && !used[base + lane];
-    const unsigned fm = __ballot_sync(0xffffffffu, fr);
-    const int r = found + __popc(fm & ((1u << lane) - 1));
-    if (fr && r < need) s_free[r] = base + lane;
-    found += __popc(fm);
-  }
-  __syncwarp();
-  for (int x = lane; x < need; x += 32) {
-    const int r = x / p.ppw, i = x % p.ppw;
-    p.table_dst[(int64_t)b * p.page_cap + s_ent[r] * p.ppw + i] = s_free[x];
+  __syncthreads();  // page-use flags complete
+  const int pper = (p.page_cap + nt - 1) / nt;
+  const int p0 = min(p.page_cap, tid * pper), p1 = min(p.page_cap, p0 + pper);
+  int fcnt = 0;
+  for (int i = p0; i < p1; ++i) fcnt += used[i] ? 0 : 1;
+  int ftot = 0;
+  int r = block_excl_scan(fcnt, s_scan, ftot);  // its barriers also publish s_ent / s_need
+  const int need = s_need;
+  for (int i = p0; i < p1 && r < need; ++i)
+    if (!used[i]) s_free[r++] = i;
+  __syncthreads();
+  for (int x = tid; x < min(need, ftot); x += nt) {  // the pool always has `need` free pages
+    const int rr = x / p.ppw, i = x % p.ppw;
+    p.table_dst[(int64_t)b * p.page_cap + s_ent[rr] * p.ppw + i] = s_free[x];
   }
 }
 
@@ -816,7 +819,7 @@ int launch_evict(EvictParams& p, cudaStream_t stream) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.B);
-  cfg.blockDim = dim3(kSelectThreads);
+  cfg.blockDim = dim3(drop ? kDropThreads : kSelectThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

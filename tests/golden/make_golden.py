@@ -346,16 +346,21 @@ def gen_cfg1_e2e_half(ref_eager):
 def _effective_scores(cache, li):
     """[1, H, W] window scores of layer ``li`` including the step's scores
     that the reference keeps pending in ``cache_kwargs`` until the next
-    update(), and the [1, W] original window ids (identity before the first
-    eviction)."""
+    update() (which may already cover a window the state does not list yet),
+    and the [1, W] original window ids: identity before the first eviction,
+    and a window that only the pending scores cover takes the id after the
+    newest one (windows are numbered in order of creation)."""
     st = cache._states[li]
     pend = cache.cache_kwargs[li].get("window_scores") if li in cache.cache_kwargs else None
     ids = st.original_window_ids
-    W = ids.shape[-1] if ids is not None else max(
-        st.window_scores.shape[-1] if st.window_scores is not None else 0,
-        pend.shape[-1] if pend is not None else 0)
+    W = max(ids.shape[-1] if ids is not None else 0,
+            st.window_scores.shape[-1] if st.window_scores is not None else 0,
+            pend.shape[-1] if pend is not None else 0)
     if ids is None:
         ids = torch.arange(W, dtype=torch.long).unsqueeze(0)
+    elif ids.shape[-1] < W:
+        extra = ids[:, -1:] + torch.arange(1, W - ids.shape[-1] + 1, dtype=ids.dtype).unsqueeze(0)
+        ids = torch.cat([ids, extra], dim=-1)
     H = (st.window_scores if st.window_scores is not None else pend).shape[1]
     eff = torch.zeros(1, H, W, dtype=torch.float32)
     for part in (st.window_scores, pend):

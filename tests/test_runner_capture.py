@@ -11,7 +11,8 @@ b200 backend with the runner's capture after every model call; every step's
 window ids, eviction flag, top-K ids and retained ids equal the reference
 eager backend's run, its window scores match within 1e-5 relative (the
 reference holds a step's scores pending until the next update(); the
-recorded reference scores include them), and the npz written from the
+recorded reference state includes them, and a window they cover before the
+state lists it), and the npz written from the
 capture equals the one written from the reference's capture.
 """
 
