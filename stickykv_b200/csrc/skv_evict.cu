@@ -540,11 +540,6 @@ __device__ void gather_block(const EvictParams& p, const ApplyGrid& a, int bid) 
       r >= 0 ? p.ids_src[(int64_t)b * p.scores_cap + r] : next_id + (j - p.R);
 }
 
-// fp tokens that stay fp, copied into the destination store with their keys
-// stripped at the old and re-applied at the new position (op by op in the
-// KV dtype).  A thread owns one (token, 16-byte vector of the first half of
-// the channels) of one row and walks the KV heads, so its cos/sin rows are
-// loaded once; it handles the vector and its rotation partner.
 // Keys of the fp tokens that stay fp, stripped at the old and re-applied at
 // the new position (op by op in the KV dtype).  A thread owns one (token,
 // 16-byte vector of the first half of the channels) of one row and walks the
