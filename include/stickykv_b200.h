@@ -72,7 +72,7 @@ typedef enum skv_dtype { SKV_F32 = 0, SKV_F16 = 1, SKV_BF16 = 2 } skv_dtype;
  *            mode: every retained token stays in kv_dtype).
  * rope       rope_cos/rope_sin [rope_positions][head_dim/2] fp32: the model
  *            rotary module's cos/sin (first half; the second half repeats it)
- *            for positions 0..rope_positions-1.
+ *            for positions 0..rope_positions-1; 16-byte aligned.
  */
 typedef struct skv_layer_desc {
   int32_t batch;

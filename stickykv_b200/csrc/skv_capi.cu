@@ -51,6 +51,9 @@ static int check_layer(const skv_layer_desc* L) {
   if (L->sink_pad != (L->num_sink + 7) / 8 * 8) return SKV_ERR_INVALID_ARG;
   if (L->fp_capacity <= 0 || !L->k_fp || !L->v_fp) return SKV_ERR_INVALID_ARG;
   if (!aligned(L->k_fp, 16) || !aligned(L->v_fp, 16)) return SKV_ERR_MISALIGNED;
+  // rope rows are read as 8- and 16-byte vectors
+  if ((L->rope_cos && !aligned(L->rope_cos, 16)) || (L->rope_sin && !aligned(L->rope_sin, 16)))
+    return SKV_ERR_MISALIGNED;
   if (L->tier_page_capacity < 0) return SKV_ERR_INVALID_ARG;
   if (L->tier_page_capacity > 0) {
     if (L->window_size % kPageTokens) return SKV_ERR_UNSUPPORTED;

@@ -194,14 +194,21 @@ struct TileRuns {
     const int c_i4 = max(0, min(i, ib) - ia), c_fp = max(0, min(i, fb) - fa);
     return kCostGeneric * (i - c_i4 - c_fp) + kCostI4 * c_i4 + kCostFp * c_fp;
   }
-  // smallest i with cost_before(i) >= target
+  // smallest i with cost_before(i) >= target (n if none): the cost grows
+  // linearly inside each class segment, so walk the five segments
   __device__ __forceinline__ int at_cost(int target) const {
-    int lo = 0, hi = n;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (cost_before(mid) >= target) hi = mid; else lo = mid + 1;
+    if (target <= 0) return 0;
+    const int end[5] = {ia, ib, fa, fb, n};
+    const int cost[5] = {kCostGeneric, kCostI4, kCostGeneric, kCostFp, kCostGeneric};
+    int start = 0, c = 0;
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+      const int seg = (end[s] - start) * cost[s];
+      if (c + seg >= target) return start + (target - c + cost[s] - 1) / cost[s];
+      c += seg;
+      start = end[s];
     }
-    return lo;
+    return n;
   }
 };
 
@@ -291,17 +298,27 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   // rq = scl * R(-P) q; with `raw` the elements e >= 2 (k-rows 8..15 of each
   // k-block, which meet the odd nibbles of the raw int4 codes, 16x larger)
   // carry an extra 1/16 (exact: a power of two)
+  // (channel pairs d, d+1 are read as one 8-byte cos/sin and one 4-byte
+  // query load each)
   auto seed = [&](int P, float scl, bool raw) {
+    union QPair { uint32_t u; T e[2]; };
 #pragma unroll
     for (int kb = 0; kb < KB / 2; ++kb)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
-        const float c = p.cos[(int64_t)P * (D / 2) + d], s = p.sin[(int64_t)P * (D / 2) + d];
-        const float x = q_live ? ld_f32(qp + d) : 0.f, y = q_live ? ld_f32(qp + d + D / 2) : 0.f;
-        const float f = (raw && e >= 2) ? scl * 0.0625f : scl;
-        rq[kb][e] = fmaf(x, c, y * s) * f;
-        rq[kb + KB / 2][e] = fmaf(y, c, -x * s) * f;
+      for (int eh = 0; eh < 2; ++eh) {
+        const int d = 16 * kb + 2 * t + 8 * eh;
+        const float2 c = *reinterpret_cast<const float2*>(p.cos + (int64_t)P * (D / 2) + d);
+        const float2 s = *reinterpret_cast<const float2*>(p.sin + (int64_t)P * (D / 2) + d);
+        QPair xq, yq;
+        xq.u = q_live ? *reinterpret_cast<const uint32_t*>(qp + d) : 0u;
+        yq.u = q_live ? *reinterpret_cast<const uint32_t*>(qp + d + D / 2) : 0u;
+        const float f = (raw && eh == 1) ? scl * 0.0625f : scl;
+        const float x0 = ld_f32(&xq.e[0]), x1 = ld_f32(&xq.e[1]);
+        const float y0 = ld_f32(&yq.e[0]), y1 = ld_f32(&yq.e[1]);
+        rq[kb][2 * eh] = fmaf(x0, c.x, y0 * s.x) * f;
+        rq[kb][2 * eh + 1] = fmaf(x1, c.y, y1 * s.y) * f;
+        rq[kb + KB / 2][2 * eh] = fmaf(y0, c.x, -x0 * s.x) * f;
+        rq[kb + KB / 2][2 * eh + 1] = fmaf(y1, c.y, -x1 * s.y) * f;
       }
   };
 
@@ -482,11 +499,18 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
 #pragma unroll
     for (int kb = 0; kb < KB / 2; ++kb)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = 16 * kb + 2 * t + (e & 1) + 8 * (e >> 1);
-        stc[kb][e] = can_step ? p.cos[kRotStep * (D / 2) + d] : 1.f;
-        sts[kb][e] = can_step ? p.sin[kRotStep * (D / 2) + d] : 0.f;
-        nst[kb][e] = -sts[kb][e];
+      for (int eh = 0; eh < 2; ++eh) {  // channels d, d+1 as one 8-byte load
+        const int d = 16 * kb + 2 * t + 8 * eh;
+        const float2 c = can_step ? *reinterpret_cast<const float2*>(p.cos + kRotStep * (D / 2) + d)
+                                  : make_float2(1.f, 1.f);
+        const float2 sn = can_step ? *reinterpret_cast<const float2*>(p.sin + kRotStep * (D / 2) + d)
+                                   : make_float2(0.f, 0.f);
+        stc[kb][2 * eh] = c.x;
+        stc[kb][2 * eh + 1] = c.y;
+        sts[kb][2 * eh] = sn.x;
+        sts[kb][2 * eh + 1] = sn.y;
+        nst[kb][2 * eh] = -sn.x;
+        nst[kb][2 * eh + 1] = -sn.y;
       }
     // query of this thread's column at the first tile
     {
@@ -773,39 +797,40 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   }
   __syncthreads();
   float* s_M = wo + kWarps * 4 * D;                 // [4]
+  float* s_fw = s_M + 4;                            // [kWarps][4]: exp2(warp max - CTA max)
   if (threadIdx.x < 4) {
     float M = -INFINITY;
     for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w * 4 + threadIdx.x]);
     s_M[threadIdx.x] = M;
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = wm[w * 4 + threadIdx.x];
+      s_fw[w * 4 + threadIdx.x] = mw == -INFINITY ? 0.f : ex2(mw - M);
+    }
   }
   __syncthreads();
   // CTA partial per head: O and sum relative to the CTA max, and the max
   for (int e = threadIdx.x; e < 4 * (D + 2); e += kThreads) {
     const int hh = e / (D + 2), c = e % (D + 2);
-    const float M = s_M[hh];
     float acc = 0.f;
     if (c == D) {
-      acc = M;
+      acc = s_M[hh];
     } else {
-      for (int w = 0; w < kWarps; ++w) {
-        const float mw = wm[w * 4 + hh];
-        if (mw == -INFINITY) continue;
-        acc += ex2(mw - M) * (c == D + 1 ? wl[w * 4 + hh] : wo[(w * 4 + hh) * D + c]);
-      }
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w)
+        acc += s_fw[w * 4 + hh] * (c == D + 1 ? wl[w * 4 + hh] : wo[(w * 4 + hh) * D + c]);
     }
     p.part[(((int64_t)b * p.Hv + kh) * p.n_split + split) * 4 * (D + 2) + e] = acc;
   }
-  const int n_units = u1 - u0;
-  {
-    // window masses of the CTA's units, relative to the CTA max
-    for (int e = threadIdx.x; e < 4 * n_units; e += kThreads) {
-      const int hh = e / n_units, k = e - hh * n_units;
-      const int u = u0 + k;
-      if (u < R.NS) continue;
-      const int i = k >> 1, h = k & 1;
-      const float mt = mass_s[i * 12 + 8 + hh];
-      const float val = (mt == -INFINITY) ? 0.f : mass_s[i * 12 + h * 4 + hh] * ex2(mt - s_M[hh]);
-      p.mass[((int64_t)b * p.Hv * 4 + kh * 4 + hh) * p.W + (u - R.NS)] = val;
+  // window masses of the CTA's units, relative to the CTA max
+  float* mrow = p.mass + ((int64_t)b * p.Hv * 4 + kh * 4) * p.W;
+  for (int k = threadIdx.x; k < u1 - u0; k += kThreads) {
+    const int u = u0 + k;
+    if (u < R.NS) continue;
+    const float* ms = mass_s + (k >> 1) * 12;
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      const float mt = ms[8 + hh];
+      mrow[(int64_t)hh * p.W + (u - R.NS)] = (mt == -INFINITY) ? 0.f : ms[(k & 1) * 4 + hh] * ex2(mt - s_M[hh]);
     }
   }
 }
