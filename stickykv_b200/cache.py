@@ -69,7 +69,7 @@ class _Side:
         self.scores: Optional[Tensor] = None
         self.ids: Optional[Tensor] = None
         self.desc: Optional[LayerDesc] = None   # ABI descriptor of this side, rebuilt when
-        self.desc_key: Optional[tuple] = None   # its buffers or the rope table change
+        self.desc_key: Optional[tuple] = None   # its buffers, the page pool or the rope table change
 
 
 class LayerState:
@@ -337,9 +337,11 @@ class WindowedCache(_HFCacheBase):
 
     def _desc(self, st: LayerState, side: _Side) -> LayerDesc:
         rope = self._rope[st.device]
-        key = (side.k.data_ptr(), side.v.data_ptr(), side.k.shape[2],
-               None if side.table is None else side.table.data_ptr(), rope[0].data_ptr())
-        if side.desc_key == key:
+        key = side.desc_key
+        # the key holds the buffers themselves: identity checks cost nothing
+        # per call, and a held buffer cannot be freed and its address reused
+        if (key is not None and key[0] is side.k and key[1] is side.v and key[2] is side.table
+                and key[3] is rope[0] and key[4] is st.pages):
             return side.desc
         r = self.resolved
         d = LayerDesc()
@@ -355,7 +357,7 @@ class WindowedCache(_HFCacheBase):
             d.tier_table = side.table.data_ptr()
         d.rope_cos, d.rope_sin = rope[0].data_ptr(), rope[1].data_ptr()
         d.rope_positions = self._rope_positions[st.device]
-        side.desc, side.desc_key = d, key
+        side.desc, side.desc_key = d, (side.k, side.v, side.table, rope[0], st.pages)
         return d
 
     def _fp_slots(self, T: int, tier_pages: int) -> int:
