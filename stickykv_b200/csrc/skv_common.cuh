@@ -6,9 +6,24 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/stickykv_b200.h"
 
 namespace skv {
+
+// Raise a kernel's dynamic shared-memory limit on the current device once:
+// `done` is the caller's per-kernel bit set of devices already configured
+// (devices 32 and up are configured on every call).
+template <typename K>
+inline void max_smem_once(std::atomic<uint32_t>& done, K kernel, int bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t bit = dev < 32 ? 1u << dev : 0u;
+  if (bit && (done.load(std::memory_order_relaxed) & bit)) return;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  done.fetch_or(bit, std::memory_order_relaxed);
+}
 
 constexpr int kPageTokens = 8;   // tokens per int4 page / per MMA half-tile
 constexpr int kQGroup = 32;      // channels per int4 scale/zero group

@@ -1021,7 +1021,8 @@ template <typename T, int D>
 int launch_mma(MmaParams& p, cudaStream_t stream) {
   using C = Cfg<D>;
   static_assert(C::kSmemBytes <= 227 * 1024, "smem");
-  cudaFuncSetAttribute(decode_mma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmemBytes);
+  static std::atomic<uint32_t> smem_set{0};
+  max_smem_once(smem_set, decode_mma_kernel<T, D>, (int)C::kSmemBytes);
   decode_mma_kernel<T, D><<<dim3(p.n_split, p.Hv, p.B), kThreads, C::kSmemBytes, stream>>>(p);
   SKV_CHECK_LAUNCH();
   cudaLaunchConfig_t cfg{};

@@ -66,6 +66,7 @@ __device__ int block_excl_scan(int v, int* smem, int& total) {
 }
 
 constexpr int kSelectThreads = 1024;
+constexpr int kSelectSmemMax = 200 * 1024;  // dynamic shared memory a select may use
 // score/id slots initialised past the retained windows at each eviction: a
 // decode step adds at most two windows before the next eviction.
 constexpr int kTailWindows = 8;
@@ -805,13 +806,14 @@ int launch_evict(EvictParams& p, cudaStream_t stream) {
   const size_t smem = drop ? (size_t)4 * p.E + 4 * ((size_t)(p.n_tier_old_tok / p.ws) * p.ppw + 1) +
                                  (p.tier ? (size_t)p.page_cap : 0) + 16
                            : select_smem_bytes(p.E, p.R, p.tier ? p.page_cap : 0);
-  if (smem > 200 * 1024) return SKV_ERR_CAPACITY;
+  if (smem > (size_t)kSelectSmemMax) return SKV_ERR_CAPACITY;
   if (partial) {  // the selects read the keys only for a partial top-k
     evict_keys_kernel<<<dim3(ceil_div(p.E, kKeysThreads), p.B), kKeysThreads, 0, stream>>>(p);
     SKV_CHECK_LAUNCH();
   }
   auto kernel = drop ? evict_select_drop_kernel : evict_select_kernel;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::atomic<uint32_t> smem_set[2];  // the radix and the few-drops select
+  max_smem_once(smem_set[drop ? 1 : 0], kernel, kSelectSmemMax);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.B);
   cfg.blockDim = dim3(drop ? kDropThreads : kSelectThreads);
