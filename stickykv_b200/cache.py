@@ -44,7 +44,16 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+# torch's own accessors of the current device and of a device's current raw
+# stream (what torch.cuda.current_device / current_stream(...).cuda_stream
+# return, without building a Stream object: they run on every native call)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_cur_dev = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def _stream(device: torch.device) -> int:
+    if _raw_stream is not None and _cur_dev is not None:
+        return _raw_stream(device.index if device.index is not None else _cur_dev())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -52,7 +61,7 @@ def _on(device: torch.device):
     """Make ``device`` current for a native call (kernels launch on the
     current device; the stream passed with them belongs to ``device``).
     Layers of one model may sit on different GPUs (``device_map``)."""
-    if device.index is None or device.index == torch.cuda.current_device():
+    if device.index is None or device.index == (_cur_dev() if _cur_dev is not None else torch.cuda.current_device()):
         return contextlib.nullcontext()
     return torch.cuda.device(device)
 
@@ -417,9 +426,9 @@ class WindowedCache(_HFCacheBase):
 
     @staticmethod
     def _kv_ok(k: Tensor, v: Tensor) -> bool:
-        es = k.element_size()
-        return (k.stride() == v.stride() and k.stride(-1) == 1 and k.data_ptr() % 16 == 0
-                and v.data_ptr() % 16 == 0 and all((x * es) % 16 == 0 for x in k.stride()[:3]))
+        es, ks = k.element_size(), k.stride()
+        return (ks == v.stride() and ks[3] == 1 and k.data_ptr() % 16 == 0 and v.data_ptr() % 16 == 0
+                and (ks[0] * es) % 16 == 0 and (ks[1] * es) % 16 == 0 and (ks[2] * es) % 16 == 0)
 
     def _defer_append(self, st: LayerState, k: Tensor, v: Tensor) -> None:
         if not self._kv_ok(k, v):
@@ -554,7 +563,8 @@ class WindowedCache(_HFCacheBase):
             st.decode_ws = L.skv_decode_workspace_size(C.byref(d), st.decode_ws_T)
         ws = self._workspace(st.decode_ws, st.device)
         # q[:, :, 0, :] and out[:, 0] by strides (no views)
-        qs_b, qs_h, os_b, os_h = query.stride(0), query.stride(1), out.stride(0), out.stride(2)
+        qst, ost = query.stride(), out.stride()
+        qs_b, qs_h, os_b, os_h = qst[0], qst[1], ost[0], ost[2]
         with _on(st.device):
             if st.pending is not None:
                 k, v = st.pending
