@@ -223,7 +223,6 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   constexpr int FP_IT = 8 * C::kCPR / 32;                 // cp.async per lane per fp tensor per unit
   constexpr int PG_CH = PB / 16;                          // 16-byte chunks per page
   constexpr int PG_IT = (PG_CH + 31) / 32;
-  constexpr int I4_IT = (2 * PG_CH + 31) / 32;            // chunks per lane for a page pair
   constexpr float kThresh = 8.f;                          // lazy rescale margin (log2 domain)
   extern __shared__ __align__(128) unsigned char smem[];
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;  // kh: query-head group
@@ -471,22 +470,16 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2) decode_mma_kernel(c
   // ======================= int4 tiles (both units pages) =======================
   auto run_int4 = [&](int i0, int i1) {
     constexpr int SL = C::kI4Slots, SB = 2 * PB;
-    auto issue = [&](int i, uint32_t dst) {
+    auto issue = [&](int i, uint32_t dst) {  // chunk 32k + lane of each page
       const int2 pr = *reinterpret_cast<const int2*>(tbl + 2 * i);
       const unsigned char* pa = pages_l + (int64_t)pr.x * PB;
       const unsigned char* pb = pages_l + (int64_t)pr.y * PB;
 #pragma unroll
-      for (int k = 0; k < I4_IT; ++k) {
-        const int c0 = 32 * k;  // chunk of lane 0
-        if (c0 + 31 < PG_CH) {
+      for (int k = 0; k < PG_IT; ++k)
+        if (32 * k + 31 < PG_CH || lane + 32 * k < PG_CH) {
           cp_async16(dst + 512 * k, pa + 512 * k);
-        } else if (c0 >= PG_CH) {
-          if (c0 + 31 < 2 * PG_CH || lane + c0 < 2 * PG_CH) cp_async16(dst + 512 * k, pb + (c0 - PG_CH) * 16);
-        } else {
-          const unsigned char* src = lane + c0 < PG_CH ? pa + 512 * k : pb + (c0 - PG_CH) * 16;
-          if (c0 + 31 < 2 * PG_CH || lane + c0 < 2 * PG_CH) cp_async16(dst + 512 * k, src);
+          cp_async16(dst + PB + 512 * k, pb + 512 * k);
         }
-      }
     };
     const uint32_t dst_l = ring_s + lane * 16;
 #pragma unroll
