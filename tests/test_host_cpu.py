@@ -96,6 +96,11 @@ def test_null_arguments_are_rejected_without_a_gpu():
                                          1.0, None, 0, 256, 1 << 20, None) == 1    # null k_new
     assert L.skv_decode_attention_append(ctypes.byref(d), 8, 0, 24, 16, 0, 0, 16, 0, 0, 16, 0, 0, 1.0,
                                          None, 0, 256, 1 << 20, None) == 3         # misaligned k_new
+    d.rope_cos, d.rope_sin = 16, 8                                                 # rope rows are vector-read
+    assert L.skv_decode_attention(ctypes.byref(d), 8, 0, 16, 0, 0, 16, 0, 0, 1.0, None, 0, 256, 1 << 20,
+                                  None) == 3
+    assert L.skv_decode_workspace_size(ctypes.byref(d), 8) == 0
+    d.rope_cos, d.rope_sin = None, None
     # prefill: null and misaligned buffers are refused before any launch
     assert L.skv_prefill_attention(ctypes.byref(d), 8, None, 16, 16, 16, 1.0, None, 0, 256, 1 << 20,
                                    None) == 1                                       # null q
