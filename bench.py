@@ -349,12 +349,12 @@ def run_ours(args, rank, world, dev):
     # e2e: the same step through the public API with host buffers inside the
     # timed region.  Each step issues, at its start, one pinned H2D copy of
     # its packed q|k|v on a copy stream into one of two device buffers (after
-    # the step that last read that buffer), and its attention waits for that
-    # copy; the attention output comes back by one D2H copy on the compute
-    # stream at the step's end.  The timed region ends after the last copy.
-    # (Both copies on the compute stream: 81 us per step at 16 rows, the H2D
-    # adding 16 us of copy latency between the kernels; both on the copy
-    # stream: host-bound on stream handoffs, 83 us.)
+    # the step that last read that buffer) and, behind it on the same stream,
+    # the D2H copy of the previous step's attention output (after that step);
+    # its attention waits for its own input copy.  The timed region ends
+    # after the last step's output is back.  (Both copies on the compute
+    # stream: 81 us per step at 16 rows, the H2D adding 16 us of copy latency
+    # between the kernels; only the H2D on the copy stream: 72 us.)
     cstream = torch.cuda.current_stream(dev)
     nq_el, nk_el = rows * HQ * D, rows * HKV * D
     nbuf = cycle
@@ -366,25 +366,41 @@ def run_ours(args, rank, world, dev):
                x[nq_el + nk_el:].view(rows, HKV, 1, D)) for x in din]
     copy_stream = torch.cuda.Stream(dev)
     h2d_done = [torch.cuda.Event() for _ in range(2)]
-    read_done = [torch.cuda.Event() for _ in range(2)]
-    for e in read_done:
+    step_done = [torch.cuda.Event() for _ in range(2)]
+    for e in step_done:
         e.record(cstream)
+    pending = []  # (output, host slot, buffer) of the step whose output is not copied back yet
+
+    def copy_back():
+        out, j, k = pending.pop()
+        copy_stream.wait_event(step_done[k])
+        hout[j].copy_(out, non_blocking=True)
+        out.record_stream(copy_stream)
 
     def e2e_step(i):
         j, k = i % nbuf, i % 2
         dq, dk, dv = dviews[k]
-        copy_stream.wait_event(read_done[k])
+        copy_stream.wait_event(step_done[k])  # the step that last read this input buffer
         with torch.cuda.stream(copy_stream):
             din[k].copy_(hin[j], non_blocking=True)
-        h2d_done[k].record(copy_stream)
+            h2d_done[k].record(copy_stream)
+            if pending:
+                copy_back()
         cstream.wait_event(h2d_done[k])
         cache.update(dk, dv, 0)
         out = cache.decode_attention(0, dq, scale)
-        read_done[k].record(cstream)
-        hout[j].copy_(out, non_blocking=True)
+        step_done[k].record(cstream)
+        pending.append((out, j, k))
+
+    def drain():
+        if pending:
+            with torch.cuda.stream(copy_stream):
+                copy_back()
+        cstream.wait_stream(copy_stream)
 
     for i in range(args.warmup):
         e2e_step(i)
+    drain()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -394,6 +410,7 @@ def run_ours(args, rank, world, dev):
         copy_stream.wait_event(e0)  # the first input copy starts inside the timed region
         for i in range(args.steps):
             e2e_step(i)
+        drain()
         e1.record(cstream)
         torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
