@@ -532,7 +532,10 @@ def cpu_step(oc, rng):
 
 
 E2E = dict(layers=16, hidden=2048, heads=32, kv_heads=8, head_dim=64, ffn=8192, theta=5e5, vocab=128256,
-           batch=32, prompt=8192, decode=256)
+           batch=32, prompt=8192, decode=256, budget=BUDGET, name="Llama-3.2-1B shape, 8k prompt")
+# the 8B-class configuration: 64 rows of 32k-token prompts, 128 greedy steps, budget 0.25
+E2E_8B = dict(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, ffn=14336, theta=5e5, vocab=128256,
+              batch=64, prompt=32768, decode=128, budget=0.25, name="Llama-3.1-8B shape, 32k prompt")
 
 
 def run_e2e(args, rank, world, dev):
@@ -554,13 +557,13 @@ def run_e2e(args, rank, world, dev):
 
     from stickykv_b200 import DecodeGraphs, WindowedCache, WindowedCacheConfig, install_score_hooks
 
-    c = dict(E2E)
+    c = dict(E2E_8B if args.e2e_8b else E2E)
     if args.e2e_prompt:
         c["prompt"] = args.e2e_prompt
     if args.e2e_decode:
         c["decode"] = args.e2e_decode
-    budget = args.e2e_budget or BUDGET
-    rows = rows_per_rank(c["batch"], world)
+    budget = args.e2e_budget or c["budget"]
+    rows = args.e2e_rows or rows_per_rank(c["batch"], world)
     cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["ffn"],
                       num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
                       num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], rope_theta=c["theta"],
@@ -647,14 +650,15 @@ def run_e2e(args, rank, world, dev):
     steps = n_timed
     total_rows = rows * world
     return {
-        "metric": "e2e decode tokens/s (Llama-3.2-1B shape, 8k prompt, int4 tier)", "unit": "tokens/s",
+        "metric": f"e2e decode tokens/s ({c['name']}, int4 tier)", "unit": "tokens/s",
         "value": total_rows * steps / (dec_ms * 1e-3), "n_gpus": world, "steps": steps,
         "ms_per_step": dec_ms / steps, "higher_is_better": True, "scaling": "strong",
         "dtype": "bf16 (int4 tier codes)", "data": "synthetic: random N(0,0.02) weights, uniform token ids",
-        "config": {"workload": "Llama-3.2-1B-shaped decoder, greedy decode through transformers with the "
-                               "windowed cache", "layers": c["layers"], "hidden": c["hidden"],
+        "config": {"workload": f"{c['name']}: decoder with random weights, greedy decode through "
+                               "transformers with the windowed cache", "layers": c["layers"], "hidden": c["hidden"],
                    "q_heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
-                   "global_batch": total_rows, "prompt": c["prompt"], "decode_steps": c["decode"],
+                   "global_batch": total_rows, "rows_per_gpu": rows, "prompt": c["prompt"],
+                   "decode_steps": c["decode"],
                    "cache_budget": budget, "retained_tokens": cache.get_seq_length(0),
                    "parallelism": f"{world} batch shards"},
         "prefill_ms": pre_ms, "ttft_ms": pre_ms, "tpot_ms": dec_ms / steps,
@@ -875,6 +879,11 @@ def main():
     ap.add_argument("--e2e-budget", type=float, default=0.0)
     ap.add_argument("--e2e-stock", action="store_true",
                     help="with --e2e: the same model through stock transformers (DynamicCache, sdpa, no eviction)")
+    ap.add_argument("--e2e-8b", action="store_true",
+                    help="with --e2e: the Llama-3.1-8B-shaped configuration (64 rows, 32k prompt, 128 steps, "
+                         "budget 0.25) instead of the Llama-3.2-1B one")
+    ap.add_argument("--e2e-rows", type=int, default=0,
+                    help="with --e2e: rows per GPU (default: the configuration's batch split over the GPUs)")
     ap.add_argument("--e2e-eager", action="store_true",
                     help="decode the model run eagerly (no CUDA-graph replay of its steps)")
     ap.add_argument("--rows", type=int, default=0,
