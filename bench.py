@@ -711,7 +711,8 @@ def run_stock_e2e(args, rank, world, dev, model, c, rows):
         "value": rows * world * steps / (dec_ms * 1e-3), "n_gpus": world, "steps": steps,
         "ms_per_step": dec_ms / steps, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
         "data": "synthetic: random N(0,0.02) weights, uniform token ids",
-        "config": {"workload": "Llama-3.2-1B-shaped decoder, greedy decode through stock transformers",
+        "config": {"workload": f"{c['name']}: decoder with random weights, greedy decode through stock "
+                               "transformers",
                    "global_batch": rows * world, "prompt": c["prompt"], "decode_steps": c["decode"],
                    "retained_tokens": cache.get_seq_length(0)},
         "prefill_ms": pre_ms, "ttft_ms": pre_ms, "tpot_ms": dec_ms / steps, "peak_mem_gib": peak / 2 ** 30,
