@@ -278,10 +278,34 @@ def run_ours(args, rank, world, dev):
     vs = torch.randn(cycle, rows, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
     stream = torch.cuda.Stream(dev)
     scale = D ** -0.5
+    # below 32k context a step's working set fits in the 126 MB L2: every
+    # timed step and decode launch then starts with a 256 MB write that
+    # flushes it, timed on its own and subtracted
+    flush = CTX < 32768
+    fbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if flush else None
 
     def step(j):
+        if flush:
+            fbuf.fill_(j)
         cache.update(ks[j], vs[j], 0)
         return cache.decode_attention(0, qs[j], scale)
+
+    def flush_ms(n):
+        """Device time of one flush write, from n of them in one graph."""
+        if not flush:
+            return 0.0
+        gf = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gf, stream=stream):
+            for i in range(n):
+                fbuf.fill_(i)
+        gf.replay()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(5):
+            gf.replay()
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        return f0.elapsed_time(f1) / (5 * n)
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -310,7 +334,9 @@ def run_ours(args, rank, world, dev):
         n_dec = 20
         gd = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gd, stream=stream):
-            for _ in range(n_dec):
+            for i in range(n_dec):
+                if flush:
+                    fbuf.fill_(i)
                 cache.decode_attention(0, qs[0], scale)
         for _ in range(2):
             gd.replay()
@@ -320,7 +346,8 @@ def run_ours(args, rank, world, dev):
             gd.replay()
         d1.record(stream)
         torch.cuda.synchronize(dev)
-        attn_ms = d0.elapsed_time(d1) / (5 * n_dec)
+        fl_ms = flush_ms(n_dec)
+        attn_ms = d0.elapsed_time(d1) / (5 * n_dec) - fl_ms
         # the timed steps: graph replays (host-launch gaps removed)
         graphs = StepGraphs(step, cycle, stream)
         graphs.replay(2 * cycle)  # the two captured cycles, untimed, on the device
@@ -341,7 +368,7 @@ def run_ours(args, rank, world, dev):
         if world > 1:
             dist.barrier()
         clocks = sampler.stop()
-        ms = t0.elapsed_time(t1)
+        ms = t0.elapsed_time(t1) - args.steps * fl_ms
         graphs.finish_cycle()
         torch.cuda.synchronize(dev)
         del graphs, gd
@@ -413,7 +440,7 @@ def run_ours(args, rank, world, dev):
         drain()
         e1.record(cstream)
         torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = e0.elapsed_time(e1)  # no flush: below 32k context these steps are host-bound
     h2d = din[0].numel() * 2
     d2h = hout[0].numel() * 2
     evict_host = float(np.mean(evict_ms)) if evict_ms else 0.0
@@ -434,11 +461,12 @@ def run_ours(args, rank, world, dev):
     step_bytes = (bytes_per_launch + evict_bytes / WS) * world
     step_achieved = step_bytes / (ms / args.steps * 1e-3) / 1e9
     # every step: decode with its fused append, then the split merge; an
-    # evicting step appends on its own and adds the select and apply kernels
-    gpu_launches = args.steps * 2 + n_evict * 3
+    # evicting step appends on its own and adds the keys, select and apply
+    # kernels
+    gpu_launches = args.steps * 2 + n_evict * 4
     traffic = None
     tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and CTX == 32768 and rows == B:  # the captured workload
         try:
             traffic = json.load(open(tp)).get("bytes_per_launch")
         except (OSError, ValueError):
@@ -454,7 +482,9 @@ def run_ours(args, rank, world, dev):
                    "context": CTX, "cache_budget": BUDGET, "window_size": WS, "sinks": SINKS, "local": LOCAL,
                    "retained_tokens": st.T, "int4_tokens": st.tier_pages * 8,
                    "evictions_in_timed_region": n_evict,
-                   "l2": "working set per step > 126 MB L2; no flush",
+                   "l2": ("a 256 MB write before every graph-timed step and decode launch flushes the "
+                          "126 MB L2 (working set below it), its time subtracted; e2e unflushed" if flush else
+                          "working set per step > 126 MB L2; no flush"),
                    "launch": "timed steps replay captured CUDA graphs (16-step cycles, single steps "
                              "for the remainder)",
                    "parallelism": f"batch partitioned over {world} GPUs ({rows} rows each), "
@@ -889,6 +919,9 @@ def main():
                     help="decode the model run eagerly (no CUDA-graph replay of its steps)")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows per GPU of the attention workload (default: the 16 rows partitioned over the GPUs)")
+    ap.add_argument("--ctx", type=int, default=0,
+                    help="context length of the decode-attention workload (default 32768; the parity tests "
+                         "cover 4096/8192/16384/32768)")
     ap.add_argument("--no-model", action="store_true",
                     help="leave the Llama-3.2-1B-shaped model run out of the default line")
     ap.add_argument("--no-tier", action="store_true",
@@ -901,6 +934,9 @@ def main():
     ap.add_argument("--prefill-head-dim", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.ctx:  # the decode-attention workload at another context length
+        globals()["CTX"] = args.ctx
+        globals()["METRIC"] = METRIC.replace("32k ctx", f"{args.ctx // 1024}k ctx")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
