@@ -143,8 +143,10 @@ def gather_logits(logits, gathered, world):
     return logits
 
 
-def build_steady_cache(dev, seed, rows=B, tier=True):
-    """A layer cache at 32k context after its first eviction (steady state)."""
+def build_steady_cache(dev, seed, rows=B, tier=True, dtype=None, ctx=None, steps=WS + 1):
+    """A layer cache at the workload's context (32k unless --ctx) after
+    `steps` decode steps: with the default nine, the ninth (generation step
+    8) runs the first eviction and the cache is in its steady state."""
     import torch
 
     from stickykv_b200 import WindowedCache, WindowedCacheConfig
@@ -165,20 +167,21 @@ def build_steady_cache(dev, seed, rows=B, tier=True):
 
     cfg = WindowedCacheConfig(window_size=WS, num_sink_tokens=SINKS, local_window_size=LOCAL,
                               cache_budget=BUDGET, int4_tier=tier)
-    cache = WindowedCache(cfg, CTX, MC(), torch.float16, RoPE(500000.0), num_layers=1, max_tokens=0)
+    dtype = dtype or torch.float16
+    ctx = ctx or CTX
+    cache = WindowedCache(cfg, ctx, MC(), dtype, RoPE(500000.0), num_layers=1, max_tokens=0)
     g = torch.Generator(device=dev).manual_seed(seed)
-    k = torch.randn(rows, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
-    v = torch.randn(rows, HKV, CTX, D, device=dev, generator=g, dtype=torch.float16)
+    k = torch.randn(rows, HKV, ctx, D, device=dev, generator=g, dtype=dtype)
+    v = torch.randn(rows, HKV, ctx, D, device=dev, generator=g, dtype=dtype)
     cache.update(k, v, 0)
     del k, v
     st = cache._states[0]
-    W = math.ceil((CTX - SINKS) / WS)
+    W = math.ceil((ctx - SINKS) / WS)
     st.sides[st.cur].scores[:, :, :W] = torch.rand(rows, HQ, W, device=dev, generator=g)
     st.has_scores, st.W, st.next_window_id = True, W, W
-    # 9 decode steps: the 9th (generation step 8) runs the first eviction
-    q = torch.randn(rows, HQ, 1, D, device=dev, generator=g, dtype=torch.float16)
-    for _ in range(WS + 1):
-        kn = torch.randn(rows, HKV, 1, D, device=dev, generator=g, dtype=torch.float16)
+    q = torch.randn(rows, HQ, 1, D, device=dev, generator=g, dtype=dtype)
+    for _ in range(steps):
+        kn = torch.randn(rows, HKV, 1, D, device=dev, generator=g, dtype=dtype)
         cache.update(kn, kn.clone(), 0)
         cache.decode_attention(0, q, D ** -0.5)
     torch.cuda.synchronize(dev)
@@ -844,6 +847,74 @@ def run_tile_profile(dev):
     return {"tile_profile": [{"seq_len": T, "tier_pages": tp, "int4_tiles": B * HKV * (tp // 2)} for T, tp in cases]}
 
 
+def first_evict_bytes(cache):
+    """HBM bytes of the cache's first eviction, which the next update()
+    runs: the accumulated scores read and the retained ones written, ids read
+    and written, the fp tokens that stay fp (sinks and local windows) read and
+    written, the kept evictable windows' K/V read and their int4 pages
+    written, the page table written."""
+    from stickykv_b200 import _lib
+    st, r = cache._states[0], cache.resolved
+    T = st.T + 1
+    W = math.ceil((T - 1 - SINKS) / WS)
+    plan = _lib.evict_plan(T, W, SINKS, WS, r.top_k_windows, cache.local_windows, cache.tier)
+    fp_kept = plan.seq_len_new - plan.tier_pages_new * 8
+    ent = plan.kept_evictable
+    rows = st.B
+    kv = rows * HKV * D * 2 * 2
+    return (rows * HQ * W * 4 + rows * HQ * plan.retained_windows * 4 + rows * (W + plan.retained_windows) * 8
+            + fp_kept * kv * 2 + ent * WS * kv + rows * HKV * ent * (WS // 8) * _lib.page_bytes(D)
+            + rows * st.page_cap * 4)
+
+
+def run_evict_first(args, dev):
+    """SURVEY config 3: the first eviction of a bf16 cache of 16384 tokens
+    (16 rows, 32/8 heads, head_dim 64, budget 0.40, int4 tier): the 613
+    kept evictable windows of every row (4904 tokens) are quantised into the
+    tier, the sinks and local windows re-rotated into the compacted store.
+    Each repetition builds a fresh cache (eight decode steps after the
+    prompt) and times its evicting update() with CUDA events: the step's
+    one-token append, the head-mean keys, the radix top-k select and the
+    apply.  The working set (the 268 MB store) exceeds the L2."""
+    import statistics
+
+    import torch
+    peak, peak_kind = measured_hbm_peak()
+    ctx, reps = 16384, max(3, min(args.steps, 10))
+    us, nbytes = [], 0
+    for rep in range(reps):
+        cache = build_steady_cache(dev, seed=1 + rep, rows=B, tier=True, dtype=torch.bfloat16, ctx=ctx, steps=WS)
+        st = cache._states[0]
+        assert cache._generation_step[0] % WS == 0 and st.tier_pages == 0
+        nbytes = first_evict_bytes(cache)
+        kn = torch.randn(B, HKV, 1, D, device=dev, dtype=torch.bfloat16)
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(s)
+        cache.update(kn, kn.clone(), 0)
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        assert st.tier_pages * 8 == cache.resolved.top_k_windows * WS  # every kept window demoted
+        us.append(e0.elapsed_time(e1) * 1e3)
+        del cache
+        torch.cuda.empty_cache()
+    med = statistics.median(us)
+    achieved = nbytes / (med * 1e-6) / 1e9
+    return {
+        "metric": "first eviction, HBM GB/s (16k ctx, bf16, int4 demotion)", "value": achieved, "unit": "GB/s",
+        "n_gpus": 1, "steps": reps, "higher_is_better": True, "us_per_eviction": med,
+        "us_all": [round(x, 1) for x in us], "algorithmic_bytes": nbytes,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind},
+        "dtype": "bf16 (int4 tier codes)", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "first eviction + re-rotation + int4 demotion of one layer", "global_batch": B,
+                   "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": ctx, "cache_budget": BUDGET,
+                   "window_size": WS, "sinks": SINKS, "local": LOCAL,
+                   "includes": "the evicting step's one-token append"},
+    }
+
+
 def run_prefill(args, dev):
     """Prompt prefill through the C-ABI (`skv_prefill_attention`: causal
     attention, log-sum-exp and the prompt's window scores) on synthetic bf16
@@ -929,6 +1000,8 @@ def main():
     ap.add_argument("--tile-profile", action="store_true",
                     help="two decode calls on the int4 part of the cache in a profiler range (for ncu)")
     ap.add_argument("--prefill", action="store_true", help="time the prompt prefill kernels instead")
+    ap.add_argument("--evict-first", action="store_true",
+                    help="time the first eviction of a bf16 16k-token cache (16 rows) instead")
     ap.add_argument("--prefill-batch", type=int, default=4)
     ap.add_argument("--prefill-len", type=int, default=8192)
     ap.add_argument("--prefill-head-dim", type=int, default=64)
@@ -957,6 +1030,8 @@ def main():
             line = run_tile_profile(dev)
         elif args.prefill:
             line = run_prefill(args, dev)
+        elif args.evict_first:
+            line = run_evict_first(args, dev)
         else:
             line = run_e2e(args, rank, world, dev) if args.e2e else run_ours(args, rank, world, dev)
         if line is not None:

@@ -65,6 +65,19 @@ __device__ int block_excl_scan(int v, int* smem, int& total) {
   return warp_off + x - v;
 }
 
+// The kept candidate windows that enter the int4 tier, by rank: at most
+// min(candidates, top-k) per row, the rest -1.  The selects write the list
+// into the row's head-mean keys, which they have read by then (and the
+// apply's demotion blocks, one per (entrant rank, page), read it).
+__host__ __device__ inline int entrant_cap_of(int E, int n_tw_old, int kprime) {
+  const int n_cand = E - n_tw_old;
+  return n_cand < kprime ? n_cand : kprime;
+}
+__device__ inline int entrant_cap(const EvictParams& p) { return entrant_cap_of(p.E, p.n_tier_old_tok / p.ws, p.kprime); }
+__device__ inline int* entrant_list(const EvictParams& p, int b) {
+  return reinterpret_cast<int*>(p.keys) + (int64_t)b * p.E;
+}
+
 constexpr int kSelectThreads = 1024;
 constexpr int kSelectSmemMax = 200 * 1024;  // dynamic shared memory a select may use
 // score/id slots initialised past the retained windows at each eviction: a
@@ -235,13 +248,18 @@ __global__ void __launch_bounds__(kSelectThreads) evict_select_kernel(EvictParam
   for (int i = p0; i < p1; ++i)
     if (!used[i]) free_list[fpos++] = i;
   __syncthreads();
+  // entrants by rank (their candidate index) for the demotion blocks, in
+  // the row's keys, which every thread has read into shared memory by now
+  int* ent = entrant_list(p, b);
   for (int j = e0; j < e1; ++j) {
     if (ret[j] >= n_tw_old) {
       for (int i = 0; i < p.ppw; ++i)
         p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + i] = free_list[epos * p.ppw + i];
+      ent[epos] = ret[j] - n_tw_old;
       ++epos;
     }
   }
+  for (int r = etot + tid; r < entrant_cap(p); r += nt) ent[r] = -1;
 }
 
 // Select for an eviction that drops only a few evictable windows (in steady
@@ -355,7 +373,12 @@ __global__ void __launch_bounds__(kDropThreads) evict_select_drop_kernel(EvictPa
       j = w - before;
     }
     const unsigned km = __ballot_sync(0xffffffffu, kept);
-    if (kept) s_ent[__popc(km & ((1u << lane) - 1))] = j;
+    const int rank = __popc(km & ((1u << lane) - 1));
+    if (kept) {
+      s_ent[rank] = j;
+      entrant_list(p, b)[rank] = lane;  // candidate n_tw_old + lane: its rank among the entrants
+    }
+    for (int r = __popc(km) + lane; r < entrant_cap(p); r += 32) entrant_list(p, b)[r] = -1;
     if (lane == 0) s_need = __popc(km) * p.ppw;  // <= 32 * 4
   }
   __syncthreads();  // page-use flags complete
@@ -485,10 +508,146 @@ __device__ void quantize_page_block(KF kin, VF vin, int pos0, const float* cos, 
 // shared scratch for quantize_page_block
 __host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D * 4 + 2 * 8 * D; }
 
+// One 32-channel group's min/max over the L lanes that hold it (N values
+// each), its fp16 scale and zero point and the N codes (quantize_page_block's
+// arithmetic).
+template <int N, int L>
+__device__ __forceinline__ void quant_lanes(const float* xv, __half& s16, __half& z16, uint8_t* out) {
+  float mn = FLT_MAX, mx = -FLT_MAX;
+#pragma unroll
+  for (int e = 0; e < N; ++e) {
+    mn = fminf(mn, xv[e]);
+    mx = fmaxf(mx, xv[e]);
+  }
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  s16 = __float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), 15.f));
+  z16 = __float2half_rn(mn);
+  const float sc = __half2float(s16), z = __half2float(z16);
+#pragma unroll
+  for (int e = 0; e < N; ++e) {
+    int c = 0;
+    if (sc != 0.f) c = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(xv[e], z), sc)), 0.f), 15.f);
+    out[e] = (uint8_t)c;
+  }
+}
+
+// The same quantisation with one warp per page (the arithmetic of
+// quantize_page_block element for element): lane t owns row r = t / 4 and a
+// quarter q = t % 4 of it -- for K the rotation pairs (c, c + D/2) with c in
+// [q D/8, (q+1) D/8), for V the channels [q D/4, (q+1) D/4) -- reads them with
+// 16-byte loads, and reduces each 32-channel group's min/max over the lanes
+// that share it.  The codes are staged in `codes` (2 * 8 * D bytes, this
+// warp's own) and packed into the fragment-order words.  `ks`/`vs` point at
+// the page's first row (rows D apart), `pos0` is its logical position.
+template <typename T, int D>
+__device__ void quantize_page_warp(const T* ks, const T* vs, int pos0, const float* cos, const float* sin,
+                                   uint8_t* page, uint8_t* codes) {
+  constexpr int half = D / 2, ng = D / kQGroup;
+  constexpr int KE = D / 8;                 // K pairs per lane
+  constexpr int VE = D / 4;                 // V channels per lane
+  constexpr int KL = kQGroup / KE;          // lanes sharing a K group (x or y part)
+  constexpr int VL = VE >= kQGroup ? 1 : kQGroup / VE;  // lanes sharing a V group
+  constexpr int EV = 16 / (int)sizeof(T);   // elements per 16-byte load
+  static_assert(KE % EV == 0 && VE % EV == 0 && KL >= 1 && (VE % kQGroup == 0 || kQGroup % VE == 0), "lanes");
+  const int lane = threadIdx.x & 31, r = lane >> 2, q = lane & 3;
+  union Vec { uint4 u; T e[EV]; };
+  uint8_t* kc = codes;
+  uint8_t* vc = codes + 8 * D;
+  {  // K: rotate the lane's pairs into the page frame, quantise the x and the y parts
+    const int c0 = q * KE;
+    float x[KE], y[KE];
+#pragma unroll
+    for (int j = 0; j < KE; j += EV) {
+      Vec a, b;
+      a.u = *reinterpret_cast<const uint4*>(ks + (int64_t)r * D + c0 + j);
+      b.u = *reinterpret_cast<const uint4*>(ks + (int64_t)r * D + c0 + j + half);
+#pragma unroll
+      for (int e = 0; e < EV; ++e) {
+        x[j + e] = Elt<T>::to_f32(a.e[e]);
+        y[j + e] = Elt<T>::to_f32(b.e[e]);
+      }
+    }
+    const int64_t pos = pos0 + r;
+#pragma unroll
+    for (int e = 0; e < KE; ++e) {
+      const int cp = c0 + e;
+      to_page_frame(x[e], y[e], cos[pos * half + cp], sin[pos * half + cp], cos[(int64_t)r * half + cp],
+                    sin[(int64_t)r * half + cp]);
+    }
+    __half s16, z16;
+    __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {  // x: channels c0.., y: c0 + half..
+      quant_lanes<KE, KL>(part ? y : x, s16, z16, kc + r * D + c0 + part * half);
+      const int gq = (c0 + part * half) / kQGroup;
+      if ((q % KL) == 0) {
+        kscl[(r * ng + gq) * 2] = s16;
+        kscl[(r * ng + gq) * 2 + 1] = z16;
+      }
+    }
+  }
+  {  // V: the lane's channels
+    const int c0 = q * VE;
+    float v[VE];
+#pragma unroll
+    for (int j = 0; j < VE; j += EV) {
+      Vec a;
+      a.u = *reinterpret_cast<const uint4*>(vs + (int64_t)r * D + c0 + j);
+#pragma unroll
+      for (int e = 0; e < EV; ++e) v[j + e] = Elt<T>::to_f32(a.e[e]);
+    }
+    __half* vscl = reinterpret_cast<__half*>(page + page_v_scales_off(D));
+    constexpr int VN = VE >= kQGroup ? kQGroup : VE;  // channels of one group on this lane
+#pragma unroll
+    for (int gs = 0; gs < VE / VN; ++gs) {
+      const int n = VN;
+      __half s16, z16;
+      quant_lanes<VN, VL>(v + gs * n, s16, z16, vc + r * D + c0 + gs * n);
+      const int gq = (c0 + gs * n) / kQGroup;
+      if ((q % VL) == 0) {
+        __half* e4 = vscl + ((r >> 1) * ng + gq) * 4;
+        e4[r & 1] = s16;
+        e4[2 + (r & 1)] = z16;
+      }
+    }
+  }
+  __syncwarp();
+  // fragment-order words: K [row][lane t][word], V [pair t][row g][word]
+  for (int idx = lane; idx < 2 * 32 * ng; idx += 32) {
+    uint32_t word = 0;
+    if (idx < 32 * ng) {
+      const int rr = idx / (4 * ng), t = (idx / ng) % 4, w = idx % ng;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ch = 2 * t + 8 * (4 * w + i);
+        word |= (uint32_t)kc[rr * D + ch] << (4 * i);
+        word |= (uint32_t)kc[rr * D + ch + 1] << (4 * (i + 4));
+      }
+      reinterpret_cast<uint32_t*>(page)[idx] = word;
+    } else {
+      const int v = idx - 32 * ng;
+      const int t = v / (8 * ng), g = (v / ng) % 8, w = v % ng;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ch = g + 8 * (4 * w + i);
+        word |= (uint32_t)vc[(2 * t) * D + ch] << (4 * i);
+        word |= (uint32_t)vc[(2 * t + 1) * D + ch] << (4 * (i + 4));
+      }
+      reinterpret_cast<uint32_t*>(page + page_v_codes_off(D))[v] = word;
+    }
+  }
+}
+
 struct ApplyGrid {
   int n_demote, n_gather, n_move, n_move_v;
   int v_runs_per_row; // value-copy runs per row: the sinks and every kept fp window
-  int demote_tasks;   // (candidate window, page) pairs per (row, kv head)
+  int demote_tasks;   // (entrant rank, page) pairs per (row, kv head)
+  int ent_cap;        // entrant ranks per row
+  int demote_pages;   // pages to demote, all rows and kv heads (head_dim >= 64: a warp each)
   int gather_chunks;  // kApplyThreads-window chunks per row
   int move_chunks;    // token chunks per row
   int k_hsplit;       // kv-head slices of the key move (more threads when few rows)
@@ -499,12 +658,28 @@ struct ApplyGrid {
 // frame and quantised (design.md:130-187).
 template <typename T, int D>
 __device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, unsigned char* smem) {
-  const int task = bid % a.demote_tasks, bh = bid / a.demote_tasks;
-  const int h = bh % p.Hkv, b = bh / p.Hkv;
+  int b, h, k, pi;
+  if constexpr (D >= 64) {  // a warp per page: (row, entrant rank, page, kv head), kv head fastest
+    const int warp = threadIdx.x >> 5;
+    int64_t pid = (int64_t)bid * (kApplyThreads / 32) + warp;
+    if (pid >= a.demote_pages) return;
+    h = (int)(pid % p.Hkv);
+    pid /= p.Hkv;
+    pi = (int)(pid % p.ppw);
+    pid /= p.ppw;
+    k = (int)(pid % a.ent_cap);
+    b = (int)(pid / a.ent_cap);
+  } else {  // a block per page
+    const int task = bid % a.demote_tasks, bh = bid / a.demote_tasks;
+    h = bh % p.Hkv;
+    b = bh / p.Hkv;
+    k = task / p.ppw;
+    pi = task % p.ppw;
+  }
   const int n_tw_old = p.n_tier_old_tok / p.ws;
-  const int cand = task / p.ppw, pi = task % p.ppw;
+  const int cand = entrant_list(p, b)[k];
+  if (cand < 0) return;  // fewer entrants in this row
   const int j = p.entrant[(int64_t)b * p.W + cand];
-  if (j < 0) return;  // candidate window dropped
   const int w = n_tw_old + cand;
   const int pos0 = p.s + w * p.ws + pi * kPageTokens;
   const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
@@ -513,9 +688,13 @@ __device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, 
   const T* vs = (const T*)p.v_src + rb;
   const int phys = p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + pi];
   uint8_t* page = p.pages + (((int64_t)b * p.Hkv + h) * p.page_cap + phys) * page_bytes(D);
-  quantize_page_block<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
-                         [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos, p.sin,
-                         page, smem);
+  if constexpr (D >= 64) {
+    quantize_page_warp<T, D>(ks, vs, pos0, p.cos, p.sin, page, smem + (threadIdx.x >> 5) * 2 * 8 * D);
+  } else {
+    quantize_page_block<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
+                           [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos, p.sin,
+                           page, smem);
+  }
 }
 
 // Score and original-id gather (cache.py:271-283) for one chunk of retained
@@ -758,8 +937,14 @@ template <typename T, int D>
 int launch_apply(EvictParams& p, cudaStream_t stream) {
   ApplyGrid a{};
   const int n_cand = p.E - p.n_tier_old_tok / p.ws;
-  a.demote_tasks = (D % kQGroup == 0 && p.tier && p.kprime > 0 && n_cand > 0) ? n_cand * p.ppw : 0;
-  a.n_demote = a.demote_tasks * p.Hkv * p.B;
+  // every (row, kv head)'s (entrant rank, page) pairs: a warp per page at
+  // head_dim 64 and 128, a block per page below
+  a.ent_cap = (D % kQGroup == 0 && p.tier && p.kprime > 0 && n_cand > 0)
+                  ? entrant_cap_of(p.E, p.n_tier_old_tok / p.ws, p.kprime)
+                  : 0;
+  a.demote_tasks = a.ent_cap * p.ppw;
+  a.demote_pages = a.demote_tasks * p.Hkv * p.B;
+  a.n_demote = D >= 64 ? ceil_div(a.demote_pages, kApplyThreads / 32) : a.demote_pages;
   a.gather_chunks = ceil_div(p.R + min(p.scores_cap - p.R, kTailWindows), kApplyThreads);
   a.n_gather = a.gather_chunks * p.B;
   a.n_fp_tok = p.T_new - p.n_tier_new_tok;  // sinks + fp windows kept
@@ -778,7 +963,7 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
   const int64_t blocks = (int64_t)a.n_demote + a.n_gather + a.n_move + a.n_move_v;
   if (blocks == 0) return SKV_OK;
   if (blocks > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
-  const size_t smem = a.n_demote ? quant_scratch_bytes(D) : 0;
+  const size_t smem = !a.n_demote ? 0 : D >= 64 ? (size_t)(kApplyThreads / 32) * 2 * 8 * D : quant_scratch_bytes(D);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)blocks);
   cfg.blockDim = dim3(kApplyThreads);
