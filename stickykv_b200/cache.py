@@ -327,8 +327,10 @@ class WindowedCache(_HFCacheBase):
             cos, sin = self.rope_module(x, pos)
         cos = cos.reshape(-1, cos.shape[-1])[:n].float()
         sin = sin.reshape(-1, sin.shape[-1])[:n].float()
-        if cos.shape[-1] != D or not torch.equal(cos[:, : D // 2], cos[:, D // 2:]) or \
-                not torch.equal(sin[:, : D // 2], sin[:, D // 2:]):
+        # the layout check reads the table back (a device sync): only when the
+        # table is first built, not when it grows during decoding
+        if cos.shape[-1] != D or (have == 0 and (not torch.equal(cos[:, : D // 2], cos[:, D // 2:]) or
+                                                not torch.equal(sin[:, : D // 2], sin[:, D // 2:]))):
             raise NotImplementedError("rotary module must use the rotate-half layout cat(f, f)")
         self._rope[dev] = (cos[:, : D // 2].contiguous(), sin[:, : D // 2].contiguous())
         self._rope_positions[dev] = n

@@ -527,10 +527,21 @@ __device__ __forceinline__ void quant_lanes(const float* xv, __half& s16, __half
   s16 = __float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), 15.f));
   z16 = __float2half_rn(mn);
   const float sc = __half2float(s16), z = __half2float(z16);
+  // code = clamp(rint((x - z) / sc)) with the quotient correctly rounded.
+  // (x - z) * (1 / sc), both products correctly rounded, is within 2^-19 of
+  // the exact quotient wherever the code is not clamped (|quotient| <= 16),
+  // so it rounds to the same integer unless it lies within 2^-17 of a
+  // half-integer; those few take the correctly rounded division.
+  const float inv = sc != 0.f ? __frcp_rn(sc) : 0.f;
 #pragma unroll
   for (int e = 0; e < N; ++e) {
     int c = 0;
-    if (sc != 0.f) c = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(xv[e], z), sc)), 0.f), 15.f);
+    if (sc != 0.f) {
+      const float t = __fsub_rn(xv[e], z);
+      float a = __fmul_rn(t, inv);
+      if (fabsf(__fsub_rn(__fsub_rn(a, floorf(a)), 0.5f)) < 0x1p-17f) a = __fdiv_rn(t, sc);
+      c = (int)fminf(fmaxf(rintf(a), 0.f), 15.f);
+    }
     out[e] = (uint8_t)c;
   }
 }
@@ -572,12 +583,16 @@ __device__ void quantize_page_warp(const T* ks, const T* vs, int pos0, const flo
       }
     }
     const int64_t pos = pos0 + r;
+    float cp_[KE], sp_[KE], c8_[KE], s8_[KE];  // the rotation rows, 16-byte loads
 #pragma unroll
-    for (int e = 0; e < KE; ++e) {
-      const int cp = c0 + e;
-      to_page_frame(x[e], y[e], cos[pos * half + cp], sin[pos * half + cp], cos[(int64_t)r * half + cp],
-                    sin[(int64_t)r * half + cp]);
+    for (int j = 0; j < KE; j += 4) {
+      *reinterpret_cast<float4*>(cp_ + j) = *reinterpret_cast<const float4*>(cos + pos * half + c0 + j);
+      *reinterpret_cast<float4*>(sp_ + j) = *reinterpret_cast<const float4*>(sin + pos * half + c0 + j);
+      *reinterpret_cast<float4*>(c8_ + j) = *reinterpret_cast<const float4*>(cos + (int64_t)r * half + c0 + j);
+      *reinterpret_cast<float4*>(s8_ + j) = *reinterpret_cast<const float4*>(sin + (int64_t)r * half + c0 + j);
     }
+#pragma unroll
+    for (int e = 0; e < KE; ++e) to_page_frame(x[e], y[e], cp_[e], sp_[e], c8_[e], s8_[e]);
     __half s16, z16;
     __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
 #pragma unroll
