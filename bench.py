@@ -12,8 +12,9 @@ larger than the 126 MB L2, so no flush is needed between steps.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 The timed steps replay one captured CUDA graph per step (the host code of a
-step runs once, at capture); `e2e` runs the same steps through the Python API
-with host buffers.  N > 1 runs as torchrun ranks, one GPU each, the 16 rows
+step runs once, at capture); `e2e` runs the same steps through the public API
+(WindowedCache stepped by DecodeGraphs) with each step's inputs copied in
+from pinned host memory and its output copied back.  N > 1 runs as torchrun ranks, one GPU each, the 16 rows
 partitioned over the ranks (strong scaling, no collective on the attention
 path); the reported value is the 16 rows decoded per second, timed as the max
 over ranks.  The default line also carries `model_e2e`: the Llama-3.2-1B
@@ -376,15 +377,16 @@ def run_ours(args, rank, world, dev):
         torch.cuda.synchronize(dev)
         del graphs, gd
 
-    # e2e: the same step through the public API with host buffers inside the
-    # timed region.  Each step issues, at its start, one pinned H2D copy of
-    # its packed q|k|v on a copy stream into one of two device buffers (after
-    # the step that last read that buffer) and, behind it on the same stream,
-    # the D2H copy of the previous step's attention output (after that step);
-    # its attention waits for its own input copy.  The timed region ends
-    # after the last step's output is back.  (Both copies on the compute
-    # stream: 81 us per step at 16 rows, the H2D adding 16 us of copy latency
-    # between the kernels; only the H2D on the copy stream: 72 us.)
+    # e2e: the same steps through the public API -- WindowedCache driven by
+    # DecodeGraphs, which replays a captured graph of each steady-state step
+    # (the call a serving loop makes) -- with host buffers inside the timed
+    # region.  Each step issues, at its start, one pinned H2D copy of its
+    # packed q|k|v on a copy stream into one of two device buffers (after the
+    # step that last read that buffer) and, behind it on the same stream, the
+    # D2H copy of the previous step's attention output (after that step); its
+    # replay waits for its own input copy.  The timed region ends after the
+    # last step's output is back.
+    from stickykv_b200 import DecodeGraphs
     cstream = torch.cuda.current_stream(dev)
     nq_el, nk_el = rows * HQ * D, rows * HKV * D
     nbuf = cycle
@@ -394,33 +396,47 @@ def run_ours(args, rank, world, dev):
     din = [torch.empty(nq_el + 2 * nk_el, device=dev, dtype=torch.float16) for _ in range(2)]
     dviews = [(x[:nq_el].view(rows, HQ, 1, D), x[nq_el:nq_el + nk_el].view(rows, HKV, 1, D),
                x[nq_el + nk_el:].view(rows, HKV, 1, D)) for x in din]
+    outs = {}  # each phase's attention output (the graph's own buffer)
+
+    def graph_step(j):
+        dq, dk, dv = dviews[j % 2]  # the period is even: a phase always reads the same buffer
+        cache.update(dk, dv, 0)
+        outs[j] = cache.decode_attention(0, dq, scale)
+
+    n_pre = 0
+    while not DecodeGraphs.ready(cache):  # to a period boundary (untimed)
+        graph_step(n_pre % cycle)
+        n_pre += 1
+    torch.cuda.synchronize(dev)
+    dgraphs = DecodeGraphs(cache, graph_step, stream=torch.cuda.Stream(dev), whole_period=False)
     copy_stream = torch.cuda.Stream(dev)
     h2d_done = [torch.cuda.Event() for _ in range(2)]
     step_done = [torch.cuda.Event() for _ in range(2)]
-    for e in step_done:
+    d2h_done = [torch.cuda.Event() for _ in range(cycle)]
+    for e in step_done + d2h_done:
         e.record(cstream)
-    pending = []  # (output, host slot, buffer) of the step whose output is not copied back yet
+    pending = []  # (phase, buffer, host slot) of the step whose output is not copied back yet
 
     def copy_back():
-        out, j, k = pending.pop()
+        j, k, slot = pending.pop()
         copy_stream.wait_event(step_done[k])
-        hout[j].copy_(out, non_blocking=True)
-        out.record_stream(copy_stream)
+        hout[slot].copy_(outs[j], non_blocking=True)
+        d2h_done[j].record(copy_stream)
 
     def e2e_step(i):
-        j, k = i % nbuf, i % 2
-        dq, dk, dv = dviews[k]
+        j = dgraphs.pos
+        k = j % 2
         copy_stream.wait_event(step_done[k])  # the step that last read this input buffer
         with torch.cuda.stream(copy_stream):
-            din[k].copy_(hin[j], non_blocking=True)
+            din[k].copy_(hin[i % nbuf], non_blocking=True)
             h2d_done[k].record(copy_stream)
             if pending:
                 copy_back()
         cstream.wait_event(h2d_done[k])
-        cache.update(dk, dv, 0)
-        out = cache.decode_attention(0, dq, scale)
+        cstream.wait_event(d2h_done[j])  # this phase's previous output has been copied back
+        dgraphs.replay(1)
         step_done[k].record(cstream)
-        pending.append((out, j, k))
+        pending.append((j, k, i % nbuf))
 
     def drain():
         if pending:
@@ -443,7 +459,8 @@ def run_ours(args, rank, world, dev):
         drain()
         e1.record(cstream)
         torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)  # no flush: below 32k context these steps are host-bound
+    e2e_ms = e0.elapsed_time(e1)  # no flush: the copies and host work of a step are part of it
+    del dgraphs
     h2d = din[0].numel() * 2
     d2h = hout[0].numel() * 2
     evict_host = float(np.mean(evict_ms)) if evict_ms else 0.0
