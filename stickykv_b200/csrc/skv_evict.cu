@@ -724,15 +724,25 @@ __device__ void gather_block(const EvictParams& p, const ApplyGrid& a, int bid) 
   const int r = j < p.R ? p.retained[(int64_t)b * p.R + j] : -1;
   const float* src = p.scores_src + (int64_t)b * p.Hq * p.scores_cap;
   float* dst = p.scores_dst + (int64_t)b * p.Hq * p.scores_cap;
-#pragma unroll 8
-  for (int h = 0; h < p.Hq; ++h)
-    dst[(int64_t)h * p.scores_cap + j] = r >= 0 ? src[(int64_t)h * p.scores_cap + r] : 0.f;
+  const int64_t* ids = p.ids_src + (int64_t)b * p.scores_cap;
   // the next window's original id is one past the newest window's (ids
   // grow by one per new window, cache.py:180-213); reading it here rather
-  // than from the host keeps a captured launch valid when replayed
-  const int64_t next_id = p.W > 0 ? p.ids_src[(int64_t)b * p.scores_cap + p.W - 1] + 1 : p.next_window_id;
-  p.ids_dst[(int64_t)b * p.scores_cap + j] =
-      r >= 0 ? p.ids_src[(int64_t)b * p.scores_cap + r] : next_id + (j - p.R);
+  // than from the host keeps a captured launch valid when replayed.  Every
+  // load of the thread (its id, the newest id, 32 heads' scores) is issued
+  // before any store, so the gather costs two memory round trips.
+  const int64_t newest = p.W > 0 ? ids[p.W - 1] : p.next_window_id - 1;
+  const int64_t id = r >= 0 ? ids[r] : 0;
+  constexpr int kH = 32;
+  for (int h0 = 0; h0 < p.Hq; h0 += kH) {
+    float v[kH];
+#pragma unroll
+    for (int i = 0; i < kH; ++i)
+      v[i] = (r >= 0 && h0 + i < p.Hq) ? src[(int64_t)(h0 + i) * p.scores_cap + r] : 0.f;
+#pragma unroll
+    for (int i = 0; i < kH; ++i)
+      if (h0 + i < p.Hq) dst[(int64_t)(h0 + i) * p.scores_cap + j] = v[i];
+  }
+  p.ids_dst[(int64_t)b * p.scores_cap + j] = r >= 0 ? id : newest + 1 + (j - p.R);
 }
 
 // Keys of the fp tokens that stay fp, stripped at the old and re-applied at
