@@ -97,12 +97,19 @@ __global__ void __launch_bounds__(kKeysThreads) evict_keys_kernel(EvictParams p)
   const float* rowp = p.scores_src + (int64_t)b * p.Hq * p.scores_cap + w;
   float acc = 0.f;
   int h = 0;
-  for (; h + 16 <= p.Hq; h += 16) {  // loads issued 16 at a time
-    float v[16];
+  for (; h + 32 <= p.Hq; h += 32) {  // loads issued 32 at a time: one round trip at 32 heads
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap];
+    for (int i = 0; i < 32; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc = __fadd_rn(acc, v[i]);
+    for (int i = 0; i < 32; ++i) acc = __fadd_rn(acc, v[i]);
+  }
+  for (; h + 8 <= p.Hq; h += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = rowp[(int64_t)(h + i) * p.scores_cap];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, v[i]);
   }
   for (; h < p.Hq; ++h) acc = __fadd_rn(acc, rowp[(int64_t)h * p.scores_cap]);
   p.keys[(int64_t)b * p.E + w] = orderable(__fdiv_rn(acc, (float)p.Hq));
