@@ -515,19 +515,28 @@ __device__ void quantize_page_block(KF kin, VF vin, int pos0, const float* cos, 
 // shared scratch for quantize_page_block
 __host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D * 4 + 2 * 8 * D; }
 
-// One 32-channel group's min/max over the L lanes that hold it (N values
-// each), its fp16 scale and zero point and the N codes (quantize_page_block's
-// arithmetic).
-template <int N, int L>
-__device__ __forceinline__ void quant_lanes(const float* xv, __half& s16, __half& z16, uint8_t* out) {
+// Codes by rounding in the float adder: for ac in [0, 15], ac + 1.5 * 2^23
+// lies in [2^23, 2^24), where floats are 1 apart, so the sum is ac rounded
+// to the nearest integer, ties to even (rintf), plus 1.5 * 2^23 -- its low
+// nibble is the code.  clamp(rint(a), 0, 15) == rint(clamp(a, 0, 15)) since
+// rint is monotone and keeps integers (a NaN clamps to 0 either way).
+constexpr float kRoundMagic = 12582912.f;
+
+// One 32-channel group held as 8 values on each of the 4 lanes of a row
+// (lanes 4r .. 4r+3): its min/max over those lanes, its fp16 scale and zero
+// point and this lane's 8 codes (quantize_page_block's arithmetic), shifted
+// into one word: with `pairs` code 2t in nibble t and code 2t+1 in nibble
+// t+4 (t < 4), else code j in nibble j.
+template <bool pairs>
+__device__ __forceinline__ uint32_t quant_group8(const float (&xv)[8], __half& s16, __half& z16) {
   float mn = FLT_MAX, mx = -FLT_MAX;
 #pragma unroll
-  for (int e = 0; e < N; ++e) {
+  for (int e = 0; e < 8; ++e) {
     mn = fminf(mn, xv[e]);
     mx = fmaxf(mx, xv[e]);
   }
 #pragma unroll
-  for (int o = 1; o < L; o <<= 1) {
+  for (int o = 1; o < 4; o <<= 1) {
     mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   }
@@ -538,129 +547,128 @@ __device__ __forceinline__ void quant_lanes(const float* xv, __half& s16, __half
   // (x - z) * (1 / sc), both products correctly rounded, is within 2^-19 of
   // the exact quotient wherever the code is not clamped (|quotient| <= 16),
   // so it rounds to the same integer unless it lies within 2^-17 of a
-  // half-integer; those few take the correctly rounded division.
+  // half-integer; those few take the correctly rounded division.  (sc == 0:
+  // every code 0.)
   const float inv = sc != 0.f ? __frcp_rn(sc) : 0.f;
+  uint32_t word = 0;
 #pragma unroll
-  for (int e = 0; e < N; ++e) {
-    int c = 0;
-    if (sc != 0.f) {
-      const float t = __fsub_rn(xv[e], z);
-      float a = __fmul_rn(t, inv);
-      if (fabsf(__fsub_rn(__fsub_rn(a, floorf(a)), 0.5f)) < 0x1p-17f) a = __fdiv_rn(t, sc);
-      c = (int)fminf(fmaxf(rintf(a), 0.f), 15.f);
-    }
-    out[e] = (uint8_t)c;
+  for (int n = 0; n < 8; ++n) {
+    const int e = pairs ? (n & 3) * 2 + (n >> 2) : n;
+    const float t = __fsub_rn(xv[e], z);
+    const float ac = fminf(fmaxf(__fmul_rn(t, inv), 0.f), 15.f);
+    float s = __fadd_rn(ac, kRoundMagic);
+    if (fabsf(__fsub_rn(ac, __fsub_rn(s, kRoundMagic))) > 0.5f - 0x1p-17f)
+      s = __fadd_rn(fminf(fmaxf(__fdiv_rn(t, sc), 0.f), 15.f), kRoundMagic);
+    word = __funnelshift_r(word, __float_as_uint(s), 4);  // the code enters at nibble 7
   }
+  return word;
+}
+
+// Butterfly transpose steps between partner lanes (lane ^ dist): the lane
+// without the `dist` bit keeps its even blocks and takes the partner's even
+// blocks into its odd ones, the other keeps its odd blocks and takes the
+// partner's odd blocks into its even ones; blocks of 16, 8 or 4 bits.
+__device__ __forceinline__ uint32_t xpose16(uint32_t x, int dist, bool odd) {
+  const uint32_t y = __shfl_xor_sync(0xffffffffu, x, dist);
+  return __byte_perm(x, y, odd ? 0x3276 : 0x5410);
+}
+__device__ __forceinline__ uint32_t xpose8(uint32_t x, int dist, bool odd) {
+  const uint32_t y = __shfl_xor_sync(0xffffffffu, x, dist);
+  return __byte_perm(x, y, odd ? 0x3715 : 0x6240);
+}
+__device__ __forceinline__ uint32_t xpose4(uint32_t x, int dist, bool odd) {
+  const uint32_t y = __shfl_xor_sync(0xffffffffu, x, dist);
+  return odd ? (x & 0xF0F0F0F0u) | ((y >> 4) & 0x0F0F0F0Fu) : (x & 0x0F0F0F0Fu) | ((y << 4) & 0xF0F0F0F0u);
 }
 
 // The same quantisation with one warp per page (the arithmetic of
-// quantize_page_block element for element): lane t owns row r = t / 4 and a
-// quarter q = t % 4 of it -- for K the rotation pairs (c, c + D/2) with c in
-// [q D/8, (q+1) D/8), for V the channels [q D/4, (q+1) D/4) -- reads them with
-// 16-byte loads, and reduces each 32-channel group's min/max over the lanes
-// that share it.  The codes are staged in `codes` (2 * 8 * D bytes, this
-// warp's own) and packed into the fragment-order words.  `ks`/`vs` point at
-// the page's first row (rows D apart), `pos0` is its logical position.
+// quantize_page_block element for element, head_dim 64 or 128): lane t owns
+// row r = t / 4 and, in every 32-channel group g, the 8 channels
+// 32g + 8q + j (q = t % 4, j < 8) -- for K the rotation pairs (c, c + D/2)
+// of the groups below D/2 -- read with 16-byte loads.  Each group's min/max
+// is reduced over the row's 4 lanes, the codes are shifted into one word per
+// group, and butterfly transposes over 4 lanes (K) or 8 lanes (V: two rows)
+// turn those into the fragment-order words, lane t writing words
+// [t * D/32, (t+1) * D/32) of each part.  `ks`/`vs` point at the page's
+// first row (rows D apart), `pos0` is its logical position.
 template <typename T, int D>
 __device__ void quantize_page_warp(const T* ks, const T* vs, int pos0, const float* cos, const float* sin,
-                                   uint8_t* page, uint8_t* codes) {
+                                   uint8_t* page) {
+  static_assert(D == 64 || D == 128, "whole 32-channel groups in each half");
   constexpr int half = D / 2, ng = D / kQGroup;
-  constexpr int KE = D / 8;                 // K pairs per lane
-  constexpr int VE = D / 4;                 // V channels per lane
-  constexpr int KL = kQGroup / KE;          // lanes sharing a K group (x or y part)
-  constexpr int VL = VE >= kQGroup ? 1 : kQGroup / VE;  // lanes sharing a V group
-  constexpr int EV = 16 / (int)sizeof(T);   // elements per 16-byte load
-  static_assert(KE % EV == 0 && VE % EV == 0 && KL >= 1 && (VE % kQGroup == 0 || kQGroup % VE == 0), "lanes");
+  constexpr int EV = 16 / (int)sizeof(T);  // elements per 16-byte load
   const int lane = threadIdx.x & 31, r = lane >> 2, q = lane & 3;
   union Vec { uint4 u; T e[EV]; };
-  uint8_t* kc = codes;
-  uint8_t* vc = codes + 8 * D;
-  {  // K: rotate the lane's pairs into the page frame, quantise the x and the y parts
-    const int c0 = q * KE;
-    float x[KE], y[KE];
+  uint32_t kw[ng], vw[ng];
+  __half ksc[ng], kzp[ng], vsc[ng], vzp[ng];
+  const int64_t pos = pos0 + r;
 #pragma unroll
-    for (int j = 0; j < KE; j += EV) {
+  for (int g = 0; g < ng / 2; ++g) {  // K: rotate the lane's pairs into the page frame
+    const int c0 = 32 * g + 8 * q;
+    float x[8], y[8], cp[8], sp[8], c8[8], s8[8];
+#pragma unroll
+    for (int j = 0; j < 8; j += EV) {
       Vec a, b;
-      a.u = *reinterpret_cast<const uint4*>(ks + (int64_t)r * D + c0 + j);
-      b.u = *reinterpret_cast<const uint4*>(ks + (int64_t)r * D + c0 + j + half);
+      a.u = *reinterpret_cast<const uint4*>(ks + r * D + c0 + j);
+      b.u = *reinterpret_cast<const uint4*>(ks + r * D + c0 + j + half);
 #pragma unroll
       for (int e = 0; e < EV; ++e) {
         x[j + e] = Elt<T>::to_f32(a.e[e]);
         y[j + e] = Elt<T>::to_f32(b.e[e]);
       }
     }
-    const int64_t pos = pos0 + r;
-    float cp_[KE], sp_[KE], c8_[KE], s8_[KE];  // the rotation rows, 16-byte loads
 #pragma unroll
-    for (int j = 0; j < KE; j += 4) {
-      *reinterpret_cast<float4*>(cp_ + j) = *reinterpret_cast<const float4*>(cos + pos * half + c0 + j);
-      *reinterpret_cast<float4*>(sp_ + j) = *reinterpret_cast<const float4*>(sin + pos * half + c0 + j);
-      *reinterpret_cast<float4*>(c8_ + j) = *reinterpret_cast<const float4*>(cos + (int64_t)r * half + c0 + j);
-      *reinterpret_cast<float4*>(s8_ + j) = *reinterpret_cast<const float4*>(sin + (int64_t)r * half + c0 + j);
+    for (int j = 0; j < 8; j += 4) {
+      *reinterpret_cast<float4*>(cp + j) = *reinterpret_cast<const float4*>(cos + pos * half + c0 + j);
+      *reinterpret_cast<float4*>(sp + j) = *reinterpret_cast<const float4*>(sin + pos * half + c0 + j);
+      *reinterpret_cast<float4*>(c8 + j) = *reinterpret_cast<const float4*>(cos + r * half + c0 + j);
+      *reinterpret_cast<float4*>(s8 + j) = *reinterpret_cast<const float4*>(sin + r * half + c0 + j);
     }
 #pragma unroll
-    for (int e = 0; e < KE; ++e) to_page_frame(x[e], y[e], cp_[e], sp_[e], c8_[e], s8_[e]);
-    __half s16, z16;
-    __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
-#pragma unroll
-    for (int part = 0; part < 2; ++part) {  // x: channels c0.., y: c0 + half..
-      quant_lanes<KE, KL>(part ? y : x, s16, z16, kc + r * D + c0 + part * half);
-      const int gq = (c0 + part * half) / kQGroup;
-      if ((q % KL) == 0) {
-        kscl[(r * ng + gq) * 2] = s16;
-        kscl[(r * ng + gq) * 2 + 1] = z16;
-      }
-    }
+    for (int e = 0; e < 8; ++e) to_page_frame(x[e], y[e], cp[e], sp[e], c8[e], s8[e]);
+    kw[g] = quant_group8<true>(x, ksc[g], kzp[g]);
+    kw[g + ng / 2] = quant_group8<true>(y, ksc[g + ng / 2], kzp[g + ng / 2]);
   }
-  {  // V: the lane's channels
-    const int c0 = q * VE;
-    float v[VE];
 #pragma unroll
-    for (int j = 0; j < VE; j += EV) {
+  for (int g = 0; g < ng; ++g) {  // V
+    const int c0 = 32 * g + 8 * q;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j += EV) {
       Vec a;
-      a.u = *reinterpret_cast<const uint4*>(vs + (int64_t)r * D + c0 + j);
+      a.u = *reinterpret_cast<const uint4*>(vs + r * D + c0 + j);
 #pragma unroll
       for (int e = 0; e < EV; ++e) v[j + e] = Elt<T>::to_f32(a.e[e]);
     }
-    __half* vscl = reinterpret_cast<__half*>(page + page_v_scales_off(D));
-    constexpr int VN = VE >= kQGroup ? kQGroup : VE;  // channels of one group on this lane
+    vw[g] = quant_group8<false>(v, vsc[g], vzp[g]);
+  }
+  // scales: lane q of each row writes group q's
+  __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
+  __half* vscl = reinterpret_cast<__half*>(page + page_v_scales_off(D));
 #pragma unroll
-    for (int gs = 0; gs < VE / VN; ++gs) {
-      const int n = VN;
-      __half s16, z16;
-      quant_lanes<VN, VL>(v + gs * n, s16, z16, vc + r * D + c0 + gs * n);
-      const int gq = (c0 + gs * n) / kQGroup;
-      if ((q % VL) == 0) {
-        __half* e4 = vscl + ((r >> 1) * ng + gq) * 4;
-        e4[r & 1] = s16;
-        e4[2 + (r & 1)] = z16;
-      }
+  for (int g = 0; g < ng; ++g) {
+    if (q == g) {
+      *reinterpret_cast<__half2*>(kscl + (r * ng + g) * 2) = __halves2half2(ksc[g], kzp[g]);
+      __half* e4 = vscl + ((r >> 1) * ng + g) * 4;
+      e4[r & 1] = vsc[g];
+      e4[2 + (r & 1)] = vzp[g];
     }
   }
-  __syncwarp();
-  // fragment-order words: K [row][lane t][word], V [pair t][row g][word]
-  for (int idx = lane; idx < 2 * 32 * ng; idx += 32) {
-    uint32_t word = 0;
-    if (idx < 32 * ng) {
-      const int rr = idx / (4 * ng), t = (idx / ng) % 4, w = idx % ng;
+  // fragment order: K word (row r, lane t, group w) takes codes 2t, 2t+1 of
+  // each of the row's 4 lanes; V word (pair t, channel g, group w) takes
+  // code g of each of the pair's 8 lanes
+  const bool o1 = lane & 1, o2 = lane & 2, o4 = lane & 4;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int ch = 2 * t + 8 * (4 * w + i);
-        word |= (uint32_t)kc[rr * D + ch] << (4 * i);
-        word |= (uint32_t)kc[rr * D + ch + 1] << (4 * (i + 4));
-      }
-      reinterpret_cast<uint32_t*>(page)[idx] = word;
-    } else {
-      const int v = idx - 32 * ng;
-      const int t = v / (8 * ng), g = (v / ng) % 8, w = v % ng;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int ch = g + 8 * (4 * w + i);
-        word |= (uint32_t)vc[(2 * t) * D + ch] << (4 * i);
-        word |= (uint32_t)vc[(2 * t + 1) * D + ch] << (4 * (i + 4));
-      }
-      reinterpret_cast<uint32_t*>(page + page_v_codes_off(D))[v] = word;
-    }
+  for (int g = 0; g < ng; ++g) {
+    kw[g] = xpose4(xpose8(kw[g], 2, o2), 1, o1);
+    vw[g] = xpose4(xpose8(xpose16(vw[g], 4, o4), 2, o2), 1, o1);
+  }
+  if constexpr (ng == 2) {
+    reinterpret_cast<uint2*>(page)[lane] = make_uint2(kw[0], kw[1]);
+    reinterpret_cast<uint2*>(page + page_v_codes_off(D))[lane] = make_uint2(vw[0], vw[1]);
+  } else {
+    reinterpret_cast<uint4*>(page)[lane] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+    reinterpret_cast<uint4*>(page + page_v_codes_off(D))[lane] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
   }
 }
 
@@ -682,15 +690,15 @@ template <typename T, int D>
 __device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, unsigned char* smem) {
   int b, h, k, pi;
   if constexpr (D >= 64) {  // a warp per page: (row, entrant rank, page, kv head), kv head fastest
-    const int warp = threadIdx.x >> 5;
-    int64_t pid = (int64_t)bid * (kApplyThreads / 32) + warp;
-    if (pid >= a.demote_pages) return;
-    h = (int)(pid % p.Hkv);
-    pid /= p.Hkv;
-    pi = (int)(pid % p.ppw);
-    pid /= p.ppw;
-    k = (int)(pid % a.ent_cap);
-    b = (int)(pid / a.ent_cap);
+    const unsigned warp = threadIdx.x >> 5;
+    unsigned pid = (unsigned)bid * (kApplyThreads / 32) + warp;  // demote_pages < 2^31
+    if (pid >= (unsigned)a.demote_pages) return;
+    h = (int)(pid % (unsigned)p.Hkv);
+    pid /= (unsigned)p.Hkv;
+    pi = (int)(pid % (unsigned)p.ppw);
+    pid /= (unsigned)p.ppw;
+    k = (int)(pid % (unsigned)a.ent_cap);
+    b = (int)(pid / (unsigned)a.ent_cap);
   } else {  // a block per page
     const int task = bid % a.demote_tasks, bh = bid / a.demote_tasks;
     h = bh % p.Hkv;
@@ -711,7 +719,7 @@ __device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, 
   const int phys = p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + pi];
   uint8_t* page = p.pages + (((int64_t)b * p.Hkv + h) * p.page_cap + phys) * page_bytes(D);
   if constexpr (D >= 64) {
-    quantize_page_warp<T, D>(ks, vs, pos0, p.cos, p.sin, page, smem + (threadIdx.x >> 5) * 2 * 8 * D);
+    quantize_page_warp<T, D>(ks, vs, pos0, p.cos, p.sin, page);
   } else {
     quantize_page_block<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
                            [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos, p.sin,
@@ -975,7 +983,9 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
                   ? entrant_cap_of(p.E, p.n_tier_old_tok / p.ws, p.kprime)
                   : 0;
   a.demote_tasks = a.ent_cap * p.ppw;
-  a.demote_pages = a.demote_tasks * p.Hkv * p.B;
+  const int64_t demote_pages = (int64_t)a.demote_tasks * p.Hkv * p.B;
+  if (demote_pages > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
+  a.demote_pages = (int)demote_pages;
   a.n_demote = D >= 64 ? ceil_div(a.demote_pages, kApplyThreads / 32) : a.demote_pages;
   a.gather_chunks = ceil_div(p.R + min(p.scores_cap - p.R, kTailWindows), kApplyThreads);
   a.n_gather = a.gather_chunks * p.B;
@@ -995,7 +1005,7 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
   const int64_t blocks = (int64_t)a.n_demote + a.n_gather + a.n_move + a.n_move_v;
   if (blocks == 0) return SKV_OK;
   if (blocks > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
-  const size_t smem = !a.n_demote ? 0 : D >= 64 ? (size_t)(kApplyThreads / 32) * 2 * 8 * D : quant_scratch_bytes(D);
+  const size_t smem = !a.n_demote || D >= 64 ? 0 : quant_scratch_bytes(D);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)blocks);
   cfg.blockDim = dim3(kApplyThreads);
