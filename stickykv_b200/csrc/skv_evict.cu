@@ -521,12 +521,14 @@ __host__ __device__ constexpr int quant_scratch_bytes(int D) { return 2 * 8 * D 
 // nibble is the code.  clamp(rint(a), 0, 15) == rint(clamp(a, 0, 15)) since
 // rint is monotone and keeps integers (a NaN clamps to 0 either way).
 constexpr float kRoundMagic = 12582912.f;
+constexpr float kNearHalf = 0.5f - 0x1p-17f;  // quotients farther than this from an integer take the exact path
 
 // One 32-channel group held as 8 values on each of the 4 lanes of a row
 // (lanes 4r .. 4r+3): its min/max over those lanes, its fp16 scale and zero
 // point and this lane's 8 codes (quantize_page_block's arithmetic), shifted
 // into one word: with `pairs` code 2t in nibble t and code 2t+1 in nibble
-// t+4 (t < 4), else code j in nibble j.
+// t+4 (t < 4), else code j in nibble j.  Lanes of the whole warp call it
+// together (its votes are warp-wide).
 template <bool pairs>
 __device__ __forceinline__ uint32_t quant_group8(const float (&xv)[8], __half& s16, __half& z16) {
   float mn = FLT_MAX, mx = -FLT_MAX;
@@ -550,16 +552,35 @@ __device__ __forceinline__ uint32_t quant_group8(const float (&xv)[8], __half& s
   // half-integer; those few take the correctly rounded division.  (sc == 0:
   // every code 0.)
   const float inv = sc != 0.f ? __frcp_rn(sc) : 0.f;
+  // Fast path: x -> (x - z) * inv (each step rounded) is monotone, so every
+  // quotient of the group lies between those of its min and max; when those
+  // lie in [-0.5, 15.5) no clamp binds.  A quotient near a half-integer, or
+  // a NaN value, sends the warp to the exact path.
+  const bool inside = __fmul_rn(__fsub_rn(mn, z), inv) >= -0.5f && __fmul_rn(__fsub_rn(mx, z), inv) < 15.5f;
   uint32_t word = 0;
+  bool redo = !inside;
+  if (__all_sync(0xffffffffu, inside)) {
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const int e = pairs ? (n & 3) * 2 + (n >> 2) : n;
-    const float t = __fsub_rn(xv[e], z);
-    const float ac = fminf(fmaxf(__fmul_rn(t, inv), 0.f), 15.f);
-    float s = __fadd_rn(ac, kRoundMagic);
-    if (fabsf(__fsub_rn(ac, __fsub_rn(s, kRoundMagic))) > 0.5f - 0x1p-17f)
-      s = __fadd_rn(fminf(fmaxf(__fdiv_rn(t, sc), 0.f), 15.f), kRoundMagic);
-    word = __funnelshift_r(word, __float_as_uint(s), 4);  // the code enters at nibble 7
+    for (int n = 0; n < 8; ++n) {
+      const int e = pairs ? (n & 3) * 2 + (n >> 2) : n;
+      const float a = __fmul_rn(__fsub_rn(xv[e], z), inv);
+      const float s = __fadd_rn(a, kRoundMagic);
+      redo |= !(fabsf(__fsub_rn(a, __fsub_rn(s, kRoundMagic))) <= kNearHalf);
+      word = __funnelshift_r(word, __float_as_uint(s), 4);  // the code enters at nibble 7
+    }
+  }
+  if (__any_sync(0xffffffffu, redo)) {  // clamped, the exact quotient near half-integers
+    word = 0;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int e = pairs ? (n & 3) * 2 + (n >> 2) : n;
+      const float t = __fsub_rn(xv[e], z);
+      const float ac = fminf(fmaxf(__fmul_rn(t, inv), 0.f), 15.f);
+      float s = __fadd_rn(ac, kRoundMagic);
+      if (fabsf(__fsub_rn(ac, __fsub_rn(s, kRoundMagic))) > kNearHalf)
+        s = __fadd_rn(fminf(fmaxf(__fdiv_rn(t, sc), 0.f), 15.f), kRoundMagic);
+      word = __funnelshift_r(word, __float_as_uint(s), 4);
+    }
   }
   return word;
 }
@@ -581,94 +602,141 @@ __device__ __forceinline__ uint32_t xpose4(uint32_t x, int dist, bool odd) {
   return odd ? (x & 0xF0F0F0F0u) | ((y >> 4) & 0x0F0F0F0Fu) : (x & 0x0F0F0F0Fu) | ((y << 4) & 0xF0F0F0F0u);
 }
 
-// The same quantisation with one warp per page (the arithmetic of
-// quantize_page_block element for element, head_dim 64 or 128): lane t owns
-// row r = t / 4 and, in every 32-channel group g, the 8 channels
-// 32g + 8q + j (q = t % 4, j < 8) -- for K the rotation pairs (c, c + D/2)
-// of the groups below D/2 -- read with 16-byte loads.  Each group's min/max
-// is reduced over the row's 4 lanes, the codes are shifted into one word per
-// group, and butterfly transposes over 4 lanes (K) or 8 lanes (V: two rows)
-// turn those into the fragment-order words, lane t writing words
-// [t * D/32, (t+1) * D/32) of each part.  `ks`/`vs` point at the page's
-// first row (rows D apart), `pos0` is its logical position.
+// Demotion warps take up to kDemoteHeadsMax kv heads of one page slot (the
+// index chain and the rotation rows read once for all of them) while that
+// still leaves kDemoteFill warps; fewer pages (a steady-state eviction) take
+// one head per warp.
+constexpr int kDemoteHeadsMax = 8;
+constexpr int kDemoteFill = 8192;
+
+// The same quantisation with one warp per page slot and `nh` kv heads (the
+// arithmetic of quantize_page_block element for element,
+// head_dim 64 or 128): lane t owns row r = t / 4 and, in every 32-channel
+// group g, the 8 channels 32g + 8q + j (q = t % 4, j < 8) -- for K the
+// rotation pairs (c, c + D/2) of the groups below D/2 -- read with 16-byte
+// loads, the next head's while this one is quantised; the rotation rows are
+// read once for all heads.  Each group's min/max is reduced over the row's 4
+// lanes, the codes are shifted into one word per group, and butterfly
+// transposes over 4 lanes (K) or 8 lanes (V: two rows) turn those into the
+// fragment-order words, lane t writing word t * D/32 + g of each part.
+// `ks`/`vs` point at the first head's page row 0 (rows D apart, heads
+// `head_elems` apart), `page` at its page (heads `head_bytes` apart); `pos0`
+// is the logical position of row 0.
 template <typename T, int D>
-__device__ void quantize_page_warp(const T* ks, const T* vs, int pos0, const float* cos, const float* sin,
-                                   uint8_t* page) {
+__device__ void quantize_pages_warp(const T* ks, const T* vs, int64_t head_elems, int nh, int pos0,
+                                    const float* cos, const float* sin, uint8_t* page, int64_t head_bytes) {
   static_assert(D == 64 || D == 128, "whole 32-channel groups in each half");
   constexpr int half = D / 2, ng = D / kQGroup;
-  constexpr int EV = 16 / (int)sizeof(T);  // elements per 16-byte load
+  constexpr int EV = 16 / (int)sizeof(T), NV = 8 / EV;  // elements per 16-byte load, loads per 8
   const int lane = threadIdx.x & 31, r = lane >> 2, q = lane & 3;
+  const bool o1 = lane & 1, o2 = lane & 2, o4 = lane & 4;
   union Vec { uint4 u; T e[EV]; };
-  uint32_t kw[ng], vw[ng];
-  __half ksc[ng], kzp[ng], vsc[ng], vzp[ng];
   const int64_t pos = pos0 + r;
 #pragma unroll
-  for (int g = 0; g < ng / 2; ++g) {  // K: rotate the lane's pairs into the page frame
+  for (int g = 0; g < ng / 2; ++g) {  // K: the lane's rotation pairs in x group g, y group g + ng/2
     const int c0 = 32 * g + 8 * q;
-    float x[8], y[8], cp[8], sp[8], c8[8], s8[8];
-#pragma unroll
-    for (int j = 0; j < 8; j += EV) {
-      Vec a, b;
-      a.u = *reinterpret_cast<const uint4*>(ks + r * D + c0 + j);
-      b.u = *reinterpret_cast<const uint4*>(ks + r * D + c0 + j + half);
-#pragma unroll
-      for (int e = 0; e < EV; ++e) {
-        x[j + e] = Elt<T>::to_f32(a.e[e]);
-        y[j + e] = Elt<T>::to_f32(b.e[e]);
-      }
-    }
+    float cp[8], sp[8];
 #pragma unroll
     for (int j = 0; j < 8; j += 4) {
       *reinterpret_cast<float4*>(cp + j) = *reinterpret_cast<const float4*>(cos + pos * half + c0 + j);
       *reinterpret_cast<float4*>(sp + j) = *reinterpret_cast<const float4*>(sin + pos * half + c0 + j);
-      *reinterpret_cast<float4*>(c8 + j) = *reinterpret_cast<const float4*>(cos + r * half + c0 + j);
-      *reinterpret_cast<float4*>(s8 + j) = *reinterpret_cast<const float4*>(sin + r * half + c0 + j);
     }
+    const T* src = ks + r * D + c0;
+    Vec nx[NV], ny[NV];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) to_page_frame(x[e], y[e], cp[e], sp[e], c8[e], s8[e]);
-    kw[g] = quant_group8<true>(x, ksc[g], kzp[g]);
-    kw[g + ng / 2] = quant_group8<true>(y, ksc[g + ng / 2], kzp[g + ng / 2]);
-  }
-#pragma unroll
-  for (int g = 0; g < ng; ++g) {  // V
-    const int c0 = 32 * g + 8 * q;
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 8; j += EV) {
-      Vec a;
-      a.u = *reinterpret_cast<const uint4*>(vs + r * D + c0 + j);
-#pragma unroll
-      for (int e = 0; e < EV; ++e) v[j + e] = Elt<T>::to_f32(a.e[e]);
+    for (int l = 0; l < NV; ++l) {
+      nx[l].u = *reinterpret_cast<const uint4*>(src + l * EV);
+      ny[l].u = *reinterpret_cast<const uint4*>(src + l * EV + half);
     }
-    vw[g] = quant_group8<false>(v, vsc[g], vzp[g]);
-  }
-  // scales: lane q of each row writes group q's
-  __half* kscl = reinterpret_cast<__half*>(page + page_k_scales_off(D));
-  __half* vscl = reinterpret_cast<__half*>(page + page_v_scales_off(D));
+#pragma unroll 1
+    for (int i = 0; i < nh; ++i) {
+      float x[8], y[8];
 #pragma unroll
-  for (int g = 0; g < ng; ++g) {
-    if (q == g) {
-      *reinterpret_cast<__half2*>(kscl + (r * ng + g) * 2) = __halves2half2(ksc[g], kzp[g]);
-      __half* e4 = vscl + ((r >> 1) * ng + g) * 4;
-      e4[r & 1] = vsc[g];
-      e4[2 + (r & 1)] = vzp[g];
+      for (int l = 0; l < NV; ++l) {
+#pragma unroll
+        for (int e = 0; e < EV; ++e) {
+          x[l * EV + e] = Elt<T>::to_f32(nx[l].e[e]);
+          y[l * EV + e] = Elt<T>::to_f32(ny[l].e[e]);
+        }
+      }
+      if (i + 1 < nh) {  // the next head's pairs load while this one is quantised
+        src += head_elems;
+#pragma unroll
+        for (int l = 0; l < NV; ++l) {
+          nx[l].u = *reinterpret_cast<const uint4*>(src + l * EV);
+          ny[l].u = *reinterpret_cast<const uint4*>(src + l * EV + half);
+        }
+      }
+      float c8[8], s8[8];  // the page-frame rows (positions 0..7): read again per head, from L1
+#pragma unroll
+      for (int j = 0; j < 8; j += 4) {
+        *reinterpret_cast<float4*>(c8 + j) = *reinterpret_cast<const float4*>(cos + r * half + c0 + j);
+        *reinterpret_cast<float4*>(s8 + j) = *reinterpret_cast<const float4*>(sin + r * half + c0 + j);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) to_page_frame(x[e], y[e], cp[e], sp[e], c8[e], s8[e]);
+      uint8_t* pg = page + i * head_bytes;
+      __half2* kscl = reinterpret_cast<__half2*>(pg + page_k_scales_off(D)) + r * ng;
+      uint32_t* kw = reinterpret_cast<uint32_t*>(pg) + lane * ng;
+      __half s16, z16;
+      uint32_t w = quant_group8<true>(x, s16, z16);
+      if (q == g) kscl[g] = __halves2half2(s16, z16);
+      kw[g] = xpose4(xpose8(w, 2, o2), 1, o1);
+      w = quant_group8<true>(y, s16, z16);
+      if (q == g + ng / 2) kscl[g + ng / 2] = __halves2half2(s16, z16);
+      kw[g + ng / 2] = xpose4(xpose8(w, 2, o2), 1, o1);
     }
   }
-  // fragment order: K word (row r, lane t, group w) takes codes 2t, 2t+1 of
-  // each of the row's 4 lanes; V word (pair t, channel g, group w) takes
-  // code g of each of the pair's 8 lanes
-  const bool o1 = lane & 1, o2 = lane & 2, o4 = lane & 4;
+  {  // V: the lane's 8 channels of every group
+    constexpr bool kPrefetch = ng * NV <= 4;  // the next head's values held as well (16 registers at most)
+    const T* src = vs + r * D + 8 * q;
+    Vec nv[ng][NV];
+    if constexpr (kPrefetch) {
 #pragma unroll
-  for (int g = 0; g < ng; ++g) {
-    kw[g] = xpose4(xpose8(kw[g], 2, o2), 1, o1);
-    vw[g] = xpose4(xpose8(xpose16(vw[g], 4, o4), 2, o2), 1, o1);
-  }
-  if constexpr (ng == 2) {
-    reinterpret_cast<uint2*>(page)[lane] = make_uint2(kw[0], kw[1]);
-    reinterpret_cast<uint2*>(page + page_v_codes_off(D))[lane] = make_uint2(vw[0], vw[1]);
-  } else {
-    reinterpret_cast<uint4*>(page)[lane] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-    reinterpret_cast<uint4*>(page + page_v_codes_off(D))[lane] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      for (int g = 0; g < ng; ++g)
+#pragma unroll
+        for (int l = 0; l < NV; ++l) nv[g][l].u = *reinterpret_cast<const uint4*>(src + 32 * g + l * EV);
+    }
+#pragma unroll 1
+    for (int i = 0; i < nh; ++i) {
+      Vec raw[ng][NV];
+#pragma unroll
+      for (int g = 0; g < ng; ++g)
+#pragma unroll
+        for (int l = 0; l < NV; ++l) {
+          if constexpr (kPrefetch) {
+            raw[g][l] = nv[g][l];
+          } else {
+            raw[g][l].u = *reinterpret_cast<const uint4*>(src + 32 * g + l * EV);
+          }
+        }
+      if (kPrefetch && i + 1 < nh) {
+#pragma unroll
+        for (int g = 0; g < ng; ++g)
+#pragma unroll
+          for (int l = 0; l < NV; ++l)
+            nv[g][l].u = *reinterpret_cast<const uint4*>(src + head_elems + 32 * g + l * EV);
+      }
+      src += head_elems;
+      uint8_t* pg = page + i * head_bytes;
+      __half* vscl = reinterpret_cast<__half*>(pg + page_v_scales_off(D)) + (r >> 1) * ng * 4;
+      uint32_t* vw = reinterpret_cast<uint32_t*>(pg + page_v_codes_off(D)) + lane * ng;
+#pragma unroll
+      for (int g = 0; g < ng; ++g) {
+        float v[8];
+#pragma unroll
+        for (int l = 0; l < NV; ++l)
+#pragma unroll
+          for (int e = 0; e < EV; ++e) v[l * EV + e] = Elt<T>::to_f32(raw[g][l].e[e]);
+        __half s16, z16;
+        const uint32_t w = quant_group8<false>(v, s16, z16);
+        if (q == g) {
+          vscl[g * 4 + (r & 1)] = s16;
+          vscl[g * 4 + 2 + (r & 1)] = z16;
+        }
+        vw[g] = xpose4(xpose8(xpose16(w, 4, o4), 2, o2), 1, o1);
+      }
+    }
   }
 }
 
@@ -677,7 +745,8 @@ struct ApplyGrid {
   int v_runs_per_row; // value-copy runs per row: the sinks and every kept fp window
   int demote_tasks;   // (entrant rank, page) pairs per (row, kv head)
   int ent_cap;        // entrant ranks per row
-  int demote_pages;   // pages to demote, all rows and kv heads (head_dim >= 64: a warp each)
+  int demote_units;   // head_dim >= 64: (row, entrant rank, page, kv-head group) warps; below: pages
+  int demote_heads;   // kv heads per demotion warp (head_dim >= 64)
   int gather_chunks;  // kApplyThreads-window chunks per row
   int move_chunks;    // token chunks per row
   int k_hsplit;       // kv-head slices of the key move (more threads when few rows)
@@ -688,13 +757,14 @@ struct ApplyGrid {
 // frame and quantised (design.md:130-187).
 template <typename T, int D>
 __device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, unsigned char* smem) {
-  int b, h, k, pi;
-  if constexpr (D >= 64) {  // a warp per page: (row, entrant rank, page, kv head), kv head fastest
-    const unsigned warp = threadIdx.x >> 5;
-    unsigned pid = (unsigned)bid * (kApplyThreads / 32) + warp;  // demote_pages < 2^31
-    if (pid >= (unsigned)a.demote_pages) return;
-    h = (int)(pid % (unsigned)p.Hkv);
-    pid /= (unsigned)p.Hkv;
+  int b, h, k, pi, nh = 1;
+  if constexpr (D >= 64) {  // a warp per (row, entrant rank, page, kv-head group), head group fastest
+    const unsigned n_hg = (unsigned)ceil_div(p.Hkv, a.demote_heads);
+    unsigned pid = (unsigned)bid * (kApplyThreads / 32) + (threadIdx.x >> 5);  // demote_units < 2^31
+    if (pid >= (unsigned)a.demote_units) return;
+    h = (int)(pid % n_hg) * a.demote_heads;
+    nh = min(a.demote_heads, p.Hkv - h);
+    pid /= n_hg;
     pi = (int)(pid % (unsigned)p.ppw);
     pid /= (unsigned)p.ppw;
     k = (int)(pid % (unsigned)a.ent_cap);
@@ -719,7 +789,8 @@ __device__ void demote_block(const EvictParams& p, const ApplyGrid& a, int bid, 
   const int phys = p.table_dst[(int64_t)b * p.page_cap + j * p.ppw + pi];
   uint8_t* page = p.pages + (((int64_t)b * p.Hkv + h) * p.page_cap + phys) * page_bytes(D);
   if constexpr (D >= 64) {
-    quantize_page_warp<T, D>(ks, vs, pos0, p.cos, p.sin, page);
+    quantize_pages_warp<T, D>(ks, vs, (int64_t)p.fp_cap_src * D, nh, pos0, p.cos, p.sin, page,
+                              (int64_t)p.page_cap * page_bytes(D));
   } else {
     quantize_page_block<D>([&](int r, int c) { return ld_f32(ks + (int64_t)r * D + c); },
                            [&](int r, int c) { return ld_f32(vs + (int64_t)r * D + c); }, pos0, p.cos, p.sin,
@@ -983,10 +1054,17 @@ int launch_apply(EvictParams& p, cudaStream_t stream) {
                   ? entrant_cap_of(p.E, p.n_tier_old_tok / p.ws, p.kprime)
                   : 0;
   a.demote_tasks = a.ent_cap * p.ppw;
-  const int64_t demote_pages = (int64_t)a.demote_tasks * p.Hkv * p.B;
-  if (demote_pages > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
-  a.demote_pages = (int)demote_pages;
-  a.n_demote = D >= 64 ? ceil_div(a.demote_pages, kApplyThreads / 32) : a.demote_pages;
+  a.demote_heads = 1;
+  if (D >= 64) {
+    const int64_t pages = (int64_t)a.demote_tasks * p.Hkv * p.B;
+    while (2 * a.demote_heads <= min(p.Hkv, kDemoteHeadsMax) && pages / (2 * a.demote_heads) >= kDemoteFill)
+      a.demote_heads *= 2;
+  }
+  const int64_t demote_units =
+      (int64_t)a.demote_tasks * (D >= 64 ? ceil_div(p.Hkv, a.demote_heads) : p.Hkv) * p.B;
+  if (demote_units > 0x7FFFFFFF) return SKV_ERR_CAPACITY;
+  a.demote_units = (int)demote_units;
+  a.n_demote = D >= 64 ? ceil_div(a.demote_units, kApplyThreads / 32) : a.demote_units;
   a.gather_chunks = ceil_div(p.R + min(p.scores_cap - p.R, kTailWindows), kApplyThreads);
   a.n_gather = a.gather_chunks * p.B;
   a.n_fp_tok = p.T_new - p.n_tier_new_tok;  // sinks + fp windows kept
