@@ -19,7 +19,9 @@ partitioned over the ranks (strong scaling, no collective on the attention
 path); the reported value is the 16 rows decoded per second, timed as the max
 over ranks.  The default line also carries `model_e2e`: the Llama-3.2-1B
 shaped decoder of run_e2e with its global batch of 32 rows partitioned over
-the ranks (skip with --no-model).
+the ranks (skip with --no-model), and at N = 1 `evict_first`: the isolated
+first eviction of a bf16 16k-token cache of run_evict_first (skip with
+--no-evict-first).
 """
 
 from __future__ import annotations
@@ -474,6 +476,9 @@ def run_ours(args, rank, world, dev):
     model = None
     if not args.no_model:
         model = run_e2e(args, rank, world, dev)
+    first = None
+    if world == 1 and not args.no_evict_first:  # the isolated first eviction, 3 repetitions
+        first = run_evict_first(argparse.Namespace(**{**vars(args), "steps": 3}), dev)
     if rank != 0:
         return None
     peak, peak_kind = measured_hbm_peak()
@@ -534,6 +539,10 @@ def run_ours(args, rank, world, dev):
     }
     if model is not None:
         line["model_e2e"] = model
+    if first is not None:
+        line["evict_first"] = {k: first[k] for k in ("metric", "value", "unit", "device_us_per_eviction",
+                                                    "host_driven_us_per_eviction", "algorithmic_bytes",
+                                                    "roofline", "config")}
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return line
@@ -1040,6 +1049,8 @@ def main():
                          "cover 4096/8192/16384/32768)")
     ap.add_argument("--no-model", action="store_true",
                     help="leave the Llama-3.2-1B-shaped model run out of the default line")
+    ap.add_argument("--no-evict-first", action="store_true",
+                    help="leave the isolated first eviction (16k bf16 cache) out of the default line")
     ap.add_argument("--no-tier", action="store_true",
                     help="keep every retained token in fp16 (reference mode) instead of the int4 tier")
     ap.add_argument("--tile-profile", action="store_true",
