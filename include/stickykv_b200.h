@@ -25,6 +25,8 @@
  *                            expand_to_token_indices policy.py:81-209,
  *                            CacheState.slice_and_keep + rerotate_keys
  *                            state.py:125-232
+ *   skv_evict_append         skv_append + skv_evict of an evicting decode
+ *                            step (state.py:68-119 + the above)
  *   skv_evict_plan_compute   the integer bookkeeping of the same block
  *                            (policy.py:108-132, :197-207)
  *   skv_prefill_scores       the prefill branch of the flash score hook
@@ -220,6 +222,20 @@ int skv_decode_attention_noalloc(const skv_layer_desc* layer, int32_t seq_len, i
 size_t skv_evict_workspace_size(const skv_layer_desc* layer, int32_t num_windows);
 int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* args,
               void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * skv_append of an evicting decode step's one token followed by skv_evict
+ * (the same block of WindowedCache.update, cache.py:230-286 after the
+ * CacheState.append of state.py:68-119), in the eviction's own launches: the
+ * token, at logical position args->seq_len - 1 (args->seq_len counts it),
+ * is kept by the local windows, so the eviction's move reads it straight
+ * from k_new / v_new ([batch][kv_heads][1][head_dim], element strides
+ * stride_b and stride_h, 16-byte aligned) into dst; it is never written to
+ * src.  dst, the scores and the ids end as after the two calls.
+ */
+int skv_evict_append(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* args,
+                     const void* k_new, const void* v_new, int64_t stride_b, int64_t stride_h,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Prefill: causal attention of q [batch][num_q_heads][T][head_dim] over

@@ -27,7 +27,7 @@ EXPORTS = (
     "skv_evict_plan_compute", "skv_append", "skv_decode_workspace_size", "skv_decode_attention",
     "skv_evict_workspace_size", "skv_evict", "skv_prefill_workspace_size",
     "skv_prefill_attention", "skv_pack_pages", "skv_decode_attention_noalloc",
-    "skv_decode_attention_append", "skv_materialize",
+    "skv_decode_attention_append", "skv_materialize", "skv_evict_append",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -86,6 +86,8 @@ def _declare(lib: C.CDLL) -> None:
         "skv_evict_workspace_size": (SZ, [C.POINTER(LayerDesc), I32]),
         "skv_evict": (C.c_int, [C.POINTER(LayerDesc), C.POINTER(LayerDesc), C.POINTER(EvictArgs),
                                 P, SZ, P]),
+        "skv_evict_append": (C.c_int, [C.POINTER(LayerDesc), C.POINTER(LayerDesc), C.POINTER(EvictArgs),
+                                       P, P, I64, I64, P, SZ, P]),
         "skv_prefill_workspace_size": (SZ, [C.POINTER(LayerDesc), I32]),
         "skv_prefill_attention": (C.c_int, [C.POINTER(LayerDesc), I32, P, P, P, P, F, P, I32, P,
                                             SZ, P]),

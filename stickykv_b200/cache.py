@@ -191,6 +191,9 @@ class WindowedCache(_HFCacheBase):
         self.telemetry = telemetry if telemetry is not None else NullTelemetry()
         self.tier = bool(config.int4_tier)
         self.local_windows = self.resolved.local_tokens // self.resolved.window_size
+        # an evicting one-token step appends inside the eviction (skv_evict_append)
+        # instead of a separate skv_append launch before it
+        self.fuse_evict_append = True
         self._states: List[LayerState] = [self._new_state() for _ in range(num_layers)]
         self._generation_step: List[int] = [0] * num_layers
         self._prefill_done: List[bool] = [False] * num_layers
@@ -416,12 +419,15 @@ class WindowedCache(_HFCacheBase):
         step = self._generation_step[layer_idx]
         ws = self.resolved.window_size
         evict = not is_prefill and step > 0 and step % ws == 0 and st.has_scores
+        fresh = None
         if not is_prefill and n_new == 1 and not evict:
             self._defer_append(st, key_states, value_states)
+        elif evict and n_new == 1 and self.fuse_evict_append:  # the token rides in the eviction
+            fresh = self._append(st, key_states, value_states, launch=False)
         else:
             self._append(st, key_states, value_states)
         if evict:
-            self._evict(st, layer_idx, step)
+            self._evict(st, layer_idx, step, fresh)
         if not is_prefill:
             self._generation_step[layer_idx] = step + 1
         return key_states, value_states
@@ -450,7 +456,10 @@ class WindowedCache(_HFCacheBase):
                                    k.stride(0), k.stride(1), k.stride(2), 1, _stream(st.device)),
                   "skv_append")
 
-    def _append(self, st: LayerState, k: Tensor, v: Tensor) -> None:
+    def _append(self, st: LayerState, k: Tensor, v: Tensor, launch: bool = True):
+        """Append n tokens; with ``launch=False`` only the bookkeeping (capacity,
+        rotary rows, length) and return the (k, v) that the eviction's
+        ``skv_evict_append`` reads the one token from."""
         n_new = k.shape[2]
         if not self._kv_ok(k, v):
             k, v = k.contiguous(), v.contiguous()
@@ -459,12 +468,14 @@ class WindowedCache(_HFCacheBase):
         self._grow_side(st, side, need)
         max_T = st.T + n_new + 2
         self._ensure_rope(max_T + 64, st.D, st.device)
-        d = self._desc(st, side)
-        with _on(st.device):
-            check(lib().skv_append(C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(),
-                                   k.stride(0), k.stride(1), k.stride(2), n_new, _stream(st.device)),
-                  "skv_append")
+        if launch:
+            d = self._desc(st, side)
+            with _on(st.device):
+                check(lib().skv_append(C.byref(d), st.T, st.tier_pages, k.data_ptr(), v.data_ptr(),
+                                       k.stride(0), k.stride(1), k.stride(2), n_new, _stream(st.device)),
+                      "skv_append")
         st.T += n_new
+        return None if launch else (k, v)
 
     def _add_scores(self, st: LayerState, new: Tensor) -> None:
         """Accumulate externally computed window scores (reference cache.py:163-228)."""
@@ -495,7 +506,7 @@ class WindowedCache(_HFCacheBase):
             st.W = W_now
 
     # -- eviction (reference cache.py:230-286) ------------------------------------------------
-    def _evict(self, st: LayerState, layer_idx: int, step: int) -> None:
+    def _evict(self, st: LayerState, layer_idx: int, step: int, fresh=None) -> None:
         r = self.resolved
         plan = _lib.evict_plan(st.T, st.W, r.num_sink_tokens, r.window_size, r.top_k_windows,
                                self.local_windows, self.tier)
@@ -526,8 +537,14 @@ class WindowedCache(_HFCacheBase):
         nbytes = lib().skv_evict_workspace_size(C.byref(ds), st.W)
         ws = self._workspace(nbytes, st.device)
         with _on(st.device):
-            check(lib().skv_evict(C.byref(ds), C.byref(dd), C.byref(a), ws.data_ptr(), ws.numel(),
-                                  _stream(st.device)), "skv_evict")
+            if fresh is None:
+                check(lib().skv_evict(C.byref(ds), C.byref(dd), C.byref(a), ws.data_ptr(), ws.numel(),
+                                      _stream(st.device)), "skv_evict")
+            else:  # this step's token, never written to src, moves into dst with the eviction
+                k, v = fresh
+                check(lib().skv_evict_append(C.byref(ds), C.byref(dd), C.byref(a), k.data_ptr(), v.data_ptr(),
+                                             k.stride(0), k.stride(1), ws.data_ptr(), ws.numel(),
+                                             _stream(st.device)), "skv_evict_append")
         if want_tel:
             ret = retained[:, : plan.retained_windows].long()
             self.telemetry.record_scores(layer_idx, step, pre, self._token_indices(ret, st.T))

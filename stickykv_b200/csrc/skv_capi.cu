@@ -246,8 +246,9 @@ size_t skv_evict_workspace_size(const skv_layer_desc* L, int32_t W) {
   return align_up((size_t)L->batch * (W > 0 ? W : 1) * 4, 256) * 3;  // retained, entrant, keys
 }
 
-int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* a,
-              void* ws, size_t ws_bytes, void* stream) {
+static int evict_impl(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* a,
+                      const void* k_new, const void* v_new, int64_t sb, int64_t sh, void* ws,
+                      size_t ws_bytes, void* stream) {
   int rc = check_layer(src);
   if (rc) return rc;
   if ((rc = check_layer(dst))) return rc;
@@ -296,7 +297,30 @@ int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_ev
   p.table_src = src->tier_table; p.table_dst = dst->tier_table; p.pages = src->tier_pages;
   p.k_src = src->k_fp; p.v_src = src->v_fp; p.k_dst = dst->k_fp; p.v_dst = dst->v_fp;
   p.cos = src->rope_cos; p.sin = src->rope_sin;
+  p.k_new = k_new; p.v_new = v_new; p.new_sb = sb; p.new_sh = sh;
   return evict_dispatch(p, (cudaStream_t)stream);
+}
+
+int skv_evict(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* a,
+              void* ws, size_t ws_bytes, void* stream) {
+  return evict_impl(src, dst, a, nullptr, nullptr, 0, 0, ws, ws_bytes, stream);
+}
+
+int skv_evict_append(const skv_layer_desc* src, const skv_layer_desc* dst, const skv_evict_args* a,
+                     const void* k_new, const void* v_new, int64_t sb, int64_t sh, void* ws,
+                     size_t ws_bytes, void* stream) {
+  int rc = check_layer(src);
+  if (rc) return rc;
+  if (!a || !k_new || !v_new || a->seq_len < 1) return SKV_ERR_INVALID_ARG;
+  const int es = elt_size(src->kv_dtype);
+  if (!aligned(k_new, 16) || !aligned(v_new, 16)) return SKV_ERR_MISALIGNED;
+  if ((sb * es) % 16 || (sh * es) % 16 || (src->head_dim * es) % 16) return SKV_ERR_MISALIGNED;
+  if (a->local_windows < 1) {  // the token need not stay fp: append it, then evict
+    if ((rc = skv_append(src, a->seq_len - 1, a->tier_pages, k_new, v_new, sb, sh, src->head_dim, 1, stream)))
+      return rc;
+    return skv_evict(src, dst, a, ws, ws_bytes, stream);
+  }
+  return evict_impl(src, dst, a, k_new, v_new, sb, sh, ws, ws_bytes, stream);
 }
 
 size_t skv_prefill_workspace_size(const skv_layer_desc* L, int32_t T) {

@@ -201,6 +201,11 @@ struct EvictParams {
   void* v_dst;
   const float* cos;
   const float* sin;
+  // this step's token when its append rides in the eviction (else null):
+  // [B][Hkv][D] with element strides new_sb, new_sh, logical position T_old - 1
+  const void* k_new;
+  const void* v_new;
+  int64_t new_sb, new_sh;
 };
 
 }  // namespace skv

@@ -861,6 +861,7 @@ __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) 
   const Geometry go{p.s, p.s_pad, p.ws, p.T_old, p.n_tier_old_tok};
   const Geometry gn{p.s, p.s_pad, p.ws, p.T_new, p.n_tier_new_tok};
   const int64_t so_slot = go.fp_slot(old_pos), sd_slot = gn.fp_slot(new_pos);
+  const bool fresh = p.k_new && old_pos == p.T_old - 1;  // this step's token: from the caller's buffer
   const float* tco = p.cos + (int64_t)old_pos * half + c0;
   const float* tso = p.sin + (int64_t)old_pos * half + c0;
   const float* tcn = p.cos + (int64_t)new_pos * half + c0;
@@ -884,8 +885,9 @@ __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) 
     }
     union V2 { uint4 u; T2 e[VE / 2]; };
     constexpr int HB = 4;  // kv heads whose loads are in flight together
-    const int64_t hs_src = (int64_t)p.fp_cap_src * D, hs_dst = (int64_t)p.fp_cap_dst * D;
-    const T* ks0 = (const T*)p.k_src + ((int64_t)b * p.Hkv * p.fp_cap_src + so_slot) * D + c0;
+    const int64_t hs_src = fresh ? p.new_sh : (int64_t)p.fp_cap_src * D, hs_dst = (int64_t)p.fp_cap_dst * D;
+    const T* ks0 = fresh ? (const T*)p.k_new + (int64_t)b * p.new_sb + c0
+                         : (const T*)p.k_src + ((int64_t)b * p.Hkv * p.fp_cap_src + so_slot) * D + c0;
     T* kd0 = (T*)p.k_dst + ((int64_t)b * p.Hkv * p.fp_cap_dst + sd_slot) * D + c0;
 #pragma unroll 1
     for (int h0 = h_begin; h0 < h_end; h0 += HB) {
@@ -923,7 +925,8 @@ __device__ void move_k_block(const EvictParams& p, const ApplyGrid& a, int bid) 
     union Vec { uint4 u; T e[VE]; };
 #pragma unroll 1
     for (int h = h_begin; h < h_end; ++h) {
-      const T* ks = (const T*)p.k_src + (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
+      const T* ks = fresh ? (const T*)p.k_new + (int64_t)b * p.new_sb + (int64_t)h * p.new_sh
+                          : (const T*)p.k_src + (((int64_t)b * p.Hkv + h) * p.fp_cap_src + so_slot) * D;
       T* kd = (T*)p.k_dst + (((int64_t)b * p.Hkv + h) * p.fp_cap_dst + sd_slot) * D;
       Vec kx, ky, ox, oy;
       kx.u = *reinterpret_cast<const uint4*>(ks + c0);
@@ -982,12 +985,17 @@ __device__ void move_v_block(const EvictParams& p, const ApplyGrid& a, int bid) 
   const T* src0 = (const T*)p.v_src + ((int64_t)b * p.Hkv * p.fp_cap_src + so_slot) * D;
   T* dst0 = (T*)p.v_dst + ((int64_t)b * p.Hkv * p.fp_cap_dst + sd_slot) * D;
   for (int c = threadIdx.x % per_unit; c < cw; c += per_unit) {
+    // this step's token (when its append rides here) comes from the caller's buffer
+    const bool fresh = p.v_new && old_pos + c / CPR == p.T_old - 1;
+    const T* sc = fresh ? (const T*)p.v_new + (int64_t)b * p.new_sb : src0;
+    const int64_t hsc = fresh ? p.new_sh : hs_src;
+    const int cc = fresh ? c % CPR : c;
     // all heads' loads first, then the stores (8 independent 16-byte loads in flight)
     for (int h0 = 0; h0 < p.Hkv; h0 += 8) {
       uint4 v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (h0 + j < p.Hkv) v[j] = reinterpret_cast<const uint4*>(src0 + (h0 + j) * hs_src)[c];
+        if (h0 + j < p.Hkv) v[j] = reinterpret_cast<const uint4*>(sc + (h0 + j) * hsc)[cc];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (h0 + j < p.Hkv) reinterpret_cast<uint4*>(dst0 + (h0 + j) * hs_dst)[c] = v[j];

@@ -552,3 +552,53 @@ def test_int4_tier_key_and_value_states_materialised(dt, D):
         np.testing.assert_array_equal(to_np(st.value_states), v)
         n += 1
     assert n == 2
+
+
+@pytest.mark.parametrize("dt,D,tier", [("f16", 64, True), ("bf16", 64, False), ("bf16", 128, True),
+                                       ("f32", 64, True)])
+def test_fused_append_evict_matches_append_then_evict(dt, D, tier):
+    """skv_evict_append (the evicting step's token read by the eviction's move,
+    never written to the source store) == skv_append + skv_evict, bit for
+    bit over three evictions: fp store, int4 tier, scores and ids."""
+    B, Hkv, G, P = 3, 2, 4, 411
+    Hq = Hkv * G
+    cos, sin = rope_tables(5e5, D, P + 64)
+    caches = []
+    for fused in (False, True):
+        g = torch.Generator().manual_seed(D + 7)
+        c = make_cache(dt, B, Hkv, Hq, D, P, 32, cos, sin, tier=tier)
+        c.fuse_evict_append = fused
+        c.update(rand((B, Hkv, P, D), dt, g).to(DEV), rand((B, Hkv, P, D), dt, g).to(DEV), 0)
+        st = c._states[0]
+        W = math.ceil((P - 4) / 8)
+        st.sides[st.cur].scores[:, :, :W] = torch.rand(B, Hq, W, generator=g).to(DEV)
+        st.has_scores, st.W, st.next_window_id = True, W, W
+        caches.append((c, g))
+    n_ev = 0
+    for step in range(25):
+        states = []
+        for c, g in caches:
+            k1 = rand((B, Hkv, 1, D), dt, g).to(DEV)
+            v1 = rand((B, Hkv, 1, D), dt, g).to(DEV)
+            sc = torch.rand(B, Hq, 1, generator=g)
+            before = c._states[0].evictions
+            c.update(k1, v1, 0)
+            st = c._states[0]
+            if st.pending is not None:
+                c._flush(st)
+            st.sides[st.cur].scores[:, :, : st.W] += sc.to(DEV)  # some mass for the next selection
+            states.append(st.evictions > before)
+        assert states[0] == states[1]
+        if states[0]:
+            n_ev += 1
+            (a, _), (b, _) = caches
+            sa, sb = a._states[0], b._states[0]
+            assert (sa.T, sa.tier_pages, sa.W) == (sb.T, sb.tier_pages, sb.W)
+            for x, y in zip(fp_parts(a), fp_parts(b)):
+                np.testing.assert_array_equal(x, y)
+            if tier:
+                for x, y in zip(tier_codes(a), tier_codes(b)):
+                    np.testing.assert_array_equal(x, y)
+            np.testing.assert_array_equal(to_np(sa.window_scores), to_np(sb.window_scores))
+            np.testing.assert_array_equal(to_np(sa.original_window_ids), to_np(sb.original_window_ids))
+    assert n_ev == 3
