@@ -486,9 +486,9 @@ def run_ours(args, rank, world, dev):
     step_bytes = (bytes_per_launch + evict_bytes / WS) * world
     step_achieved = step_bytes / (ms / args.steps * 1e-3) / 1e9
     # every step: decode with its fused append, then the split merge; an
-    # evicting step appends on its own and adds the keys, select and apply
-    # kernels
-    gpu_launches = args.steps * 2 + n_evict * 4
+    # evicting step adds the keys, select and apply kernels (its append rides
+    # in the apply)
+    gpu_launches = args.steps * 2 + n_evict * 3
     traffic = None
     tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tp) and CTX == 32768 and rows == B:  # the captured workload
@@ -529,7 +529,7 @@ def run_ours(args, rank, world, dev):
                   "frac": evict_bytes / (evict_avg * 1e-3) / 1e9 / peak if evict_avg else None,
                   "host_driven_us": evict_host * 1e3,
                   "note": "GPU time per eviction = (ms_per_step - decode launch) x window_size from the graph-timed "
-                          "steps (append + select + apply, select overlapped by the apply's moves); "
+                          "steps (keys + select + apply with the step's append, select overlapped by the apply's moves); "
                           "host_driven_us: events around an evicting update() called from Python"},
         "host_us_per_step": host_us,
         "e2e": {"value": rows * world * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
@@ -900,8 +900,9 @@ def run_evict_first(args, dev):
     are quantised into the tier, the sinks and local windows re-rotated into
     the compacted store.  Each repetition builds a fresh cache (eight decode
     steps after the prompt) and times its evicting update() with CUDA
-    events: the step's one-token append, the head-mean keys, the radix top-k
-    select and the apply -- once as called from Python on an idle stream
+    events: the head-mean keys, the radix top-k select and the apply (which
+    also moves the step's one token into the compacted store) -- once as
+    called from Python on an idle stream
     (host-driven) and once enqueued behind a sleep kernel (device time, the
     line's value).  The working set (the 268 MB store) exceeds the L2."""
     import statistics
@@ -965,7 +966,7 @@ def run_evict_first(args, dev):
         "config": {"workload": "first eviction + re-rotation + int4 demotion of one layer", "global_batch": B,
                    "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": ctx, "cache_budget": BUDGET,
                    "window_size": WS, "sinks": SINKS, "local": LOCAL,
-                   "includes": "the evicting step's one-token append"},
+                   "includes": "the evicting step's one-token append (inside the apply)"},
     }
 
 
