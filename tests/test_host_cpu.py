@@ -96,6 +96,19 @@ def test_null_arguments_are_rejected_without_a_gpu():
                                          1.0, None, 0, 256, 1 << 20, None) == 1    # null k_new
     assert L.skv_decode_attention_append(ctypes.byref(d), 8, 0, 24, 16, 0, 0, 16, 0, 0, 16, 0, 0, 1.0,
                                          None, 0, 256, 1 << 20, None) == 3         # misaligned k_new
+    # the eviction with this step's token: its buffers are checked before the eviction's own checks
+    assert L.skv_evict_append(None, None, None, 16, 16, 0, 0, None, 0, None) == 1
+    a = _lib.EvictArgs()
+    a.seq_len, a.local_windows = 9, 1
+    assert L.skv_evict_append(ctypes.byref(d), ctypes.byref(d), None, 16, 16, 0, 0, None, 0, None) == 1
+    assert L.skv_evict_append(ctypes.byref(d), ctypes.byref(d), ctypes.byref(a), None, 16, 0, 0, None, 0,
+                              None) == 1                                            # null k_new
+    assert L.skv_evict_append(ctypes.byref(d), ctypes.byref(d), ctypes.byref(a), 16, 24, 0, 0, None, 0,
+                              None) == 3                                            # misaligned v_new
+    assert L.skv_evict_append(ctypes.byref(d), ctypes.byref(d), ctypes.byref(a), 16, 16, 3, 0, None, 0,
+                              None) == 3                                            # row stride not 16 B
+    assert L.skv_evict_append(ctypes.byref(d), ctypes.byref(d), ctypes.byref(a), 16, 16, 64, 64, None, 0,
+                              None) == 1                                            # src == dst stores
     d.rope_cos, d.rope_sin = 16, 8                                                 # rope rows are vector-read
     assert L.skv_decode_attention(ctypes.byref(d), 8, 0, 16, 0, 0, 16, 0, 0, 1.0, None, 0, 256, 1 << 20,
                                   None) == 3
