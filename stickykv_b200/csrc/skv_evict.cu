@@ -614,8 +614,9 @@ constexpr int kDemoteFill = 8192;
 // head_dim 64 or 128): lane t owns row r = t / 4 and, in every 32-channel
 // group g, the 8 channels 32g + 8q + j (q = t % 4, j < 8) -- for K the
 // rotation pairs (c, c + D/2) of the groups below D/2 -- read with 16-byte
-// loads, the next head's while this one is quantised; the rotation rows are
-// read once for all heads.  Each group's min/max is reduced over the row's 4
+// loads, the next head's while this one is quantised; the rotation rows of
+// the tokens' positions are read once for all heads (the page-frame rows
+// again per head, from L1).  Each group's min/max is reduced over the row's 4
 // lanes, the codes are shifted into one word per group, and butterfly
 // transposes over 4 lanes (K) or 8 lanes (V: two rows) turn those into the
 // fragment-order words, lane t writing word t * D/32 + g of each part.
@@ -1056,8 +1057,8 @@ template <typename T, int D>
 int launch_apply(EvictParams& p, cudaStream_t stream) {
   ApplyGrid a{};
   const int n_cand = p.E - p.n_tier_old_tok / p.ws;
-  // every (row, kv head)'s (entrant rank, page) pairs: a warp per page at
-  // head_dim 64 and 128, a block per page below
+  // every (row, kv head)'s (entrant rank, page) pairs: a warp per page slot
+  // and demote_heads kv heads at head_dim 64 and 128, a block per page below
   a.ent_cap = (D % kQGroup == 0 && p.tier && p.kprime > 0 && n_cand > 0)
                   ? entrant_cap_of(p.E, p.n_tier_old_tok / p.ws, p.kprime)
                   : 0;
